@@ -1,0 +1,334 @@
+"""Benchmark: batch-1 Whisper-large-v3-turbo, 30 s clip, greedy decode forced to 224 tokens.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one full batch-1 transcription of a 30 s synthetic clip: GPU log-mel,
+32-layer encoder + cross-K/V, 4 prompt steps and 223 further greedy decode steps (EOS ignored), with
+seeded random-init weights of the large-v3-turbo architecture (no checkpoint offline).
+
+Printed metric (BASELINE.json `metric`): batch-1 30 s-clip E2E latency in ms (lower is better).
+`value` is the device time of a step with the waveform already resident in HBM (CUDA events around
+K back-to-back steps, max over ranks); `e2e` times the public API `CustomModel.transcribe(audio)`
+from pinned host audio to host token ids. Extra keys give per-token decode us, encoder / mel ms,
+the HBM roofline of the decode step and of the LM-head kernel, and the CPU baseline.
+
+N > 1 (torchrun): every rank runs its own independent clip stream on its own GPU (batch-1 decode does
+not shard; nothing crosses GPUs). The process group is used only for the barrier and the max-over-
+ranks timing reduction outside the timed region.
+
+--impl reference times the reference's own CPU path (custom/pytorch_model.py's greedy loop restated
+for CPU fp32 by oracle/hf_cpu.py) on the host cores on the same config, one bounded sample per step.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SECONDS = 30.0
+N_TOKENS = 224
+PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
+
+
+def peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {'hbm_gbs': d['hbm_gbs'], 'bf16_tflops': d['bf16_tflops'], 'source': 'measured'}
+    return dict(PEAKS_FALLBACK, source='fallback')
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for ln in getattr(self, 'lines', []):
+            parts = [p.strip() for p in ln.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == 'active':
+                    reasons.add(name)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unavailable']}
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def decode_bytes_per_token(dims, length):
+    """Algorithmic HBM bytes of one decode step at self-attention length `length`."""
+    d, f, L = dims.d_model, dims.ffn, dims.decoder_layers
+    per_layer = 2 * (3 * d * d + 3 * d + 3 * d * d + 3 * d + 2 * f * d + f + d + 6 * d)  # weights + biases + LN
+    cross = L * 2 * dims.heads * dims.enc_len * dims.head_dim * 2
+    self_kv = L * 2 * dims.heads * length * dims.head_dim * 2
+    lm = dims.vocab * d * 2 + dims.vocab * 1 + 2 * d * 2
+    emb = 2 * d * 2
+    return L * per_layer + cross + self_kv + lm + emb
+
+
+def cpu_reference_sample(n_tokens=8, threads=None):
+    """CPU fp32 reference path on a bounded sample: full mel + encoder + n_tokens decode steps.
+
+    Returns (e2e_ms extrapolated to N_TOKENS, details)."""
+    from flash_whisper_b200.audio import synthetic_audio
+    from flash_whisper_b200.weights import TURBO, load_hf_model, random_state_dict
+    from oracle.hf_cpu import transcribe_cpu
+    if threads:
+        torch.set_num_threads(threads)
+    model = load_hf_model(random_state_dict(0, TURBO), TURBO)
+    audio = synthetic_audio(0, SECONDS)
+    transcribe_cpu(model, audio[:16000], TURBO, n_tokens=2)  # warm-up (allocator, kernels)
+    return model, audio
+
+
+def run_cpu_sample(model, audio, n_tokens):
+    from flash_whisper_b200.weights import TURBO
+    from oracle.hf_cpu import transcribe_cpu
+    _, t = transcribe_cpu(model, audio, TURBO, n_tokens=n_tokens, begin_suppress=TURBO.begin_suppress)
+    per_tok = t['decode_s'] / max(1, t['n_tokens'])
+    e2e_ms = (t['mel_s'] + t['encoder_s'] + per_tok * N_TOKENS) * 1e3
+    return e2e_ms, t
+
+
+def bench_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    threads = torch.get_num_threads()
+    model, audio = cpu_reference_sample(threads=threads)
+    n_sample = 8
+    for _ in range(max(0, min(args.warmup, 1))):
+        run_cpu_sample(model, audio, n_sample)
+    vals, details = [], []
+    for _ in range(args.steps):
+        v, t = run_cpu_sample(model, audio, n_sample)
+        vals.append(v)
+        details.append(t)
+    value = statistics.median(vals)
+    sample = (f'each step: CPU fp32 log-mel + 32-layer encoder of one 30 s clip + {n_sample} greedy decode steps; '
+              f'E2E extrapolated to {N_TOKENS} tokens as mel + encoder + {N_TOKENS} x measured per-token time')
+    line = {
+        'impl': 'reference', 'metric': 'batch-1 30s-clip E2E latency', 'value': round(value, 3), 'unit': 'ms',
+        'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(value, 3),
+        'higher_is_better': False, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'config': {'workload': 'BASELINE config 3 on the CPU path (config 0 loop): 30 s clip, 224 forced tokens',
+                   'model': 'whisper-large-v3-turbo architecture, random-init seed 0', 'batch': 1,
+                   'tokens': N_TOKENS},
+        'cpu_baseline': {'value': round(value, 3), 'unit': 'ms', 'cores': threads, 'kind': 'port', 'sample': sample,
+                         'host_cpus': os.cpu_count()},
+        'e2e': {'value': round(value, 3), 'unit': 'ms', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+        'stages_ms': {k: round(statistics.median(d[k] for d in details) * 1e3, 3)
+                      for k in ('mel_s', 'encoder_s')},
+        'decode_ms_per_token': round(statistics.median(d['decode_s'] / d['n_tokens'] for d in details) * 1e3, 3),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_ours(args, rank, world, local_rank):
+    from flash_whisper_b200.audio import synthetic_audio
+    from flash_whisper_b200.model import CustomModel
+    from flash_whisper_b200.weights import TURBO, random_state_dict
+
+    torch.cuda.set_device(local_rank)
+    dims = TURBO
+    model = CustomModel(state_dict=random_state_dict(0, dims), dims=dims, selftest=False)
+    audio = synthetic_audio(rank, SECONDS)
+    model.wave.copy_(torch.from_numpy(audio))
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def maxed(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device='cuda')
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t)
+
+    for _ in range(args.warmup):
+        model.decode_device(N_TOKENS)
+    torch.cuda.synchronize()
+
+    # (1) device time of a full step, inputs resident in HBM
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.decode_device(N_TOKENS)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    step_ms = maxed(e0.elapsed_time(e1) / args.steps)
+    toks = model.tokens[:N_TOKENS].tolist()
+
+    # (2) stage breakdown: mel, encoder, prompt, decode per token
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    reps = max(3, args.steps)
+    mel_ms = enc_ms = dec_ms = 0.0
+    n_chunks = -(-(N_TOKENS - 1) // model.chunk)
+    for _ in range(reps):
+        ev[0].record(stream)
+        model.run_mel()
+        ev[1].record(stream)
+        model.run_encoder()
+        ev[2].record(stream)
+        model.run_prompt()
+        ev[3].record(stream)
+        for _ in range(n_chunks):
+            model.run_chunk()
+        ev[4].record(stream)
+        torch.cuda.synchronize()
+        mel_ms += ev[0].elapsed_time(ev[1]) / reps
+        enc_ms += ev[1].elapsed_time(ev[2]) / reps
+        dec_ms += ev[3].elapsed_time(ev[4]) / reps
+    dec_steps = n_chunks * model.chunk
+    us_per_token = maxed(dec_ms * 1e3 / dec_steps)
+
+    # (3) LM-head kernel alone (the largest single kernel of the decode step), same stream
+    lm_iters = 50
+    ext = model.ext
+    best = torch.zeros(1, dtype=torch.long, device='cuda')
+    for _ in range(3):
+        ext.lm_head_argmax(model.h, model.dec.lm_head, model.base_mask, best)
+        best.zero_()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(lm_iters):
+        ext.lm_head_argmax(model.h, model.dec.lm_head, model.base_mask, best)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    lm_us = e0.elapsed_time(e1) * 1e3 / lm_iters
+
+    # (4) end to end through the public API: pinned host audio -> host token ids
+    for _ in range(2):
+        model.transcribe(audio, max_new_tokens=N_TOKENS, stop_at_eos=False)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = model.transcribe(audio, max_new_tokens=N_TOKENS, stop_at_eos=False)
+    e2e_ms = maxed((time.perf_counter() - t0) * 1e3 / args.steps)
+    barrier()
+    assert out['token_ids'] == toks, 'public API and device path disagree'
+
+    pk = peaks()
+    avg_len = 4 + N_TOKENS / 2
+    step_bytes = decode_bytes_per_token(dims, int(avg_len))
+    lm_bytes = dims.vocab * dims.d_model * 2 + dims.vocab + dims.d_model * 2
+    lm_gbs = lm_bytes / (lm_us * 1e-6) / 1e9
+    dec_gbs = step_bytes / (us_per_token * 1e-6) / 1e9
+    launches_per_step = 2 + (2 + 7 * dims.encoder_layers + 2) + 34 * (4 + dec_steps)
+    line = {
+        'metric': 'batch-1 30s-clip E2E latency', 'value': round(step_ms, 4), 'unit': 'ms', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(step_ms, 4), 'higher_is_better': False,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f16', 'data': 'synthetic',
+        'config': {'workload': 'BASELINE config 3: GPU log-mel + graphed 32-layer encoder + graphed 4-layer decoder, '
+                               '30 s clip, greedy forced to 224 tokens',
+                   'model': 'whisper-large-v3-turbo architecture, random-init seed 0 (fp16)', 'global_batch': world,
+                   'seq_len': N_TOKENS, 'parallelism': f'replicas{world}' if world > 1 else 'single',
+                   'l2': 'working set larger than L2 (347 MB per decode step, 1.26 GB encoder weights)'},
+        'e2e': {'value': round(e2e_ms, 4), 'unit': 'ms', 'h2d_bytes_per_step': 480000 * 4,
+                'd2h_bytes_per_step': N_TOKENS * 8},
+        'decode_us_per_token': round(us_per_token, 3),
+        'stages_ms': {'mel': round(mel_ms, 4), 'encoder': round(enc_ms, 4), 'decode': round(dec_ms, 4)},
+        'throughput_audio_s_per_s': round(world * SECONDS / (step_ms / 1e3), 2),
+        'roofline': {'bound': 'hbm', 'kernel': 'lm_head_argmax (GEMV 51866x1280 + argmax)',
+                     'achieved': round(lm_gbs, 1), 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
+                     'frac': round(lm_gbs / pk['hbm_gbs'], 4), 'traffic': None, 'peak_source': pk['source'],
+                     'launch_us': round(lm_us, 3), 'bytes_per_launch': lm_bytes},
+        'roofline_decode_step': {'bound': 'hbm', 'achieved': round(dec_gbs, 1), 'peak': pk['hbm_gbs'],
+                                 'unit': 'GB/s', 'frac': round(dec_gbs / pk['hbm_gbs'], 4),
+                                 'bytes_per_token': step_bytes},
+        'gpu_launches': launches_per_step * args.steps,
+        'clocks': clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu_model, cpu_audio = cpu_reference_sample()
+            v, t = run_cpu_sample(cpu_model, cpu_audio, 8)
+            line['cpu_baseline'] = {
+                'value': round(v, 3), 'unit': 'ms', 'cores': torch.get_num_threads(), 'kind': 'port',
+                'sample': 'CPU fp32 log-mel + encoder of one 30 s clip + 8 decode steps (oracle/hf_cpu.py, the '
+                          'custom/pytorch_model.py loop), E2E extrapolated to 224 tokens'}
+        except Exception as exc:  # the baseline is reported, never required
+            line['cpu_baseline'] = {'value': None, 'unit': 'ms', 'error': f'{type(exc).__name__}: {exc}'}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument('--gpus', type=int, default=1)
+    parser.add_argument('--steps', type=int, default=10)
+    parser.add_argument('--warmup', type=int, default=3)
+    parser.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    parser.add_argument('--no-cpu-baseline', action='store_true')
+    args = parser.parse_args()
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    if args.impl == 'reference':
+        return bench_reference(args, rank, world)
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=600),
+                                             device_id=torch.device('cuda', local_rank))
+    try:
+        return bench_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == '__main__':
+    sys.exit(main())

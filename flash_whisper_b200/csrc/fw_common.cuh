@@ -1,0 +1,182 @@
+// Shared device helpers for the flash_whisper_b200 kernels (sm_100a only).
+//
+// Everything here is plain CUDA C++ plus a little inline PTX for the Blackwell/Hopper-era
+// features the kernels lean on: mbarriers, bulk (TMA 1-D) copies global->shared, and
+// programmatic dependent launch (griddepcontrol). Every wait in this file is bounded by a
+// %globaltimer deadline so that a logic error turns into an error status, never a hung GPU.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/flash_whisper.h"
+
+namespace fw {
+
+constexpr int kHidden = 1280;   // Whisper-large-v3-turbo d_model
+constexpr int kHeadDim = 64;
+constexpr int kSplitKeys = 64;  // keys per attention split (custom/selftest.py:13)
+constexpr int kFfn = 5120;
+
+// Device-side error word, one per translation unit; fw_device_error() on the host reads them.
+// Bit layout: FW_DEVERR_* from flash_whisper.h.
+#define FW_DEFINE_ERROR_WORD() static __device__ unsigned int g_fw_dev_error = 0u
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Spin-waits give up after this many nanoseconds (two seconds).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Order-preserving (score, index) key: a larger u64 is a larger score, and equal scores
+// rank the lower index higher (torch.argmax picks the first maximum). Zero means "none".
+// Same packing as custom/kernels/whisper_kernels.cu:22-26.
+__device__ __forceinline__ unsigned long long pack_score(float v, int idx) {
+  unsigned int u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<unsigned int>(idx));
+}
+
+__device__ __forceinline__ int unpack_index(unsigned long long key) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<unsigned int>(key & 0xFFFFFFFFull));
+}
+
+// Order-preserving float <-> uint map for atomicMax on floats of either sign.
+__device__ __forceinline__ unsigned int float_to_ordered(float v) {
+  unsigned int u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ordered_to_float(unsigned int u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with the PDL attribute may start while the
+// previous kernel in the stream is still running. Before pdl_wait() it may only read data that
+// no in-flight kernel writes (weights, caches written by earlier steps); pdl_wait() blocks until
+// the previous grid has completed and its memory is visible. Every kernel here calls
+// pdl_trigger() only after its own pdl_wait(), so at most two grids overlap and the pre-wait
+// region of grid N never races with grid N-2.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------
+// mbarrier + bulk copy (1-D TMA) helpers.
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase. Returns false (and the caller records an error) if the
+// phase does not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// Bulk async copy global -> shared (this CTA), completion signalled on `bar` by byte count.
+// Both addresses must be 16-byte aligned and `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Same, with an L2 evict-first hint for data that is streamed exactly once per step.
+__device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gsrc, unsigned bytes, uint64_t* bar,
+                                                uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// fp16 helpers ------------------------------------------------------------------------------
+__device__ __forceinline__ float round_half(float v) { return __half2float(__float2half(v)); }
+
+// Exact-erf GELU on an fp32 value (F.gelu default, approximate='none').
+__device__ __forceinline__ float gelu_erf(float x) {
+  return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+}  // namespace fw
+
+// Host-side launch helper: cudaLaunchKernelEx with the programmatic-stream-serialization
+// attribute when `pdl` is set. Kernels launched this way must call fw::pdl_wait() before reading
+// anything the previous kernel writes.
+#ifdef __CUDACC__
+#include <utility>
+namespace fw {
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+}  // namespace fw
+#endif

@@ -1,0 +1,777 @@
+// Whisper encoder on B200: tcgen05/TMEM GEMMs fed by TMA, an implicit-GEMM Conv1d front end,
+// row LayerNorm and a tensor-core flash-attention kernel.
+//
+// The reference runs the HF WhisperEncoder (transformers modeling_whisper.py WhisperEncoder /
+// WhisperEncoderLayer: conv1+GELU, conv2+GELU, + sinusoid positions, 32 pre-LN layers, final LN)
+// followed by one cross-K/V GEMM for all decoder layers (custom/model.py:143-147). Here:
+//
+//  * gemm_tc_kernel: C[128 x BN] tile per CTA. Warp 0 issues TMA loads (128B-swizzled K-major
+//    tiles) into a STAGES-deep shared-memory ring, warp 1 allocates TMEM and issues
+//    tcgen05.mma (M=128, N=BN, K=16, fp16 in / fp32 accumulate in TMEM), warps 2-5 read the
+//    accumulator back with tcgen05.ld and run the fused epilogue (bias, GELU, residual add,
+//    positions, q scaling, cross-K/V scatter). Weight tiles of the first stages are requested
+//    before the PDL wait.
+//  * Conv1d(k=3, pad=1) runs as the same GEMM: the time-major input carries one zero row at each
+//    end and a 3-D tensor map [rows/stride, stride, C] lets the producer fetch tap j of output rows
+//    t0..t0+127 (input rows stride*t + j) as one box, so no im2col buffer is materialised.
+//  * enc_attention_kernel: bidirectional attention, 128 queries x one head per CTA, online
+//    softmax over 64-key blocks, QK^T and PV on mma.sync m16n8k16 with ldmatrix from swizzled
+//    shared memory, K/V double-buffered with cp.async.
+#include <cuda.h>
+
+#include "fw_common.cuh"
+#include "fw_host.h"
+
+namespace fw {
+
+FW_DEFINE_ERROR_WORD();
+
+__device__ __forceinline__ void enc_flag(unsigned bits) { atomicOr(&g_fw_dev_error, bits); }
+
+// ------------------------------------------------------------------------------------------------
+// tcgen05 / TMA wrappers
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA with 128-byte
+// swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset), descriptor
+// version 1 (sm_100), layout type 2 (SWIZZLE_128B). The leading byte offset is unused for
+// swizzled K-major tiles. Advancing K by 16 fp16 elements adds 32 bytes to the start address.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16: D f32 (bits 4-5 = 1), A and B f16 (bits 7-12 = 0),
+// both K-major (bits 15/16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ------------------------------------------------------------------------------------------------
+// GEMM
+struct GemmEpi {
+  const half* bias;
+  half* C;
+  int64_t ldc;
+  const half* R;
+  int64_t ldr;
+  int M;
+  int N;
+  int mode;
+  float scale;
+  int scale_cols;
+};
+
+__device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int n, const uint32_t (&r)[16]) {
+  float o[16];
+  float bias[16];
+  if (ep.bias) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(ep.bias + n);
+    const uint4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+    const half* bh0 = reinterpret_cast<const half*>(&b0);
+    const half* bh1 = reinterpret_cast<const half*>(&b1);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      bias[j] = __half2float(bh0[j]);
+      bias[8 + j] = __half2float(bh1[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) bias[j] = 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j] = round_half(__uint_as_float(r[j]) + bias[j]);
+
+  half* dst;
+  if (ep.mode == FW_EPI_CROSS_KV) {
+    dst = ep.C + (static_cast<size_t>(n >> 6) * ep.M + row) * 64 + (n & 63);
+  } else {
+    dst = ep.C + static_cast<size_t>(row) * ep.ldc + n;
+  }
+  if (ep.mode == FW_EPI_BIAS_GELU) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = gelu_erf(o[j]);
+  } else if (ep.mode == FW_EPI_BIAS_RESID || ep.mode == FW_EPI_GELU_POS) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(ep.R + static_cast<size_t>(row) * ep.ldr + n);
+    const uint4 a0 = r4[0], a1 = r4[1];
+    const half* rh0 = reinterpret_cast<const half*>(&a0);
+    const half* rh1 = reinterpret_cast<const half*>(&a1);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float res = __half2float(j < 8 ? rh0[j] : rh1[j - 8]);
+      o[j] = ep.mode == FW_EPI_GELU_POS ? round_half(gelu_erf(o[j])) + res : res + o[j];
+    }
+  } else if (ep.mode == FW_EPI_BIAS_SCALE) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (n + j < ep.scale_cols) o[j] = o[j] * ep.scale;
+  }
+  uint4 w0, w1;
+  half2* h0 = reinterpret_cast<half2*>(&w0);
+  half2* h1 = reinterpret_cast<half2*>(&w1);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    h0[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+    h1[j] = __floats2half2_rn(o[8 + 2 * j], o[8 + 2 * j + 1]);
+  }
+  reinterpret_cast<uint4*>(dst)[0] = w0;
+  reinterpret_cast<uint4*>(dst)[1] = w1;
+}
+
+template <int BN, int STAGES, bool kConv>
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                         const __grid_constant__ CUtensorMap tmB, int num_kb,
+                                                         int conv_c, int conv_stride, GemmEpi ep) {
+  constexpr int BM = 128, BK = 64;
+  constexpr uint32_t kABytes = BM * BK * 2;
+  constexpr uint32_t kBBytes = BN * BK * 2;
+  constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tmem_bar;
+  __shared__ uint32_t tmem_base_sh;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&tmem_bar, 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int pre = num_kb < STAGES ? num_kb : STAGES;
+      for (int kb = 0; kb < pre; ++kb) {  // weight tiles do not depend on the previous kernel
+        mbar_arrive_expect_tx(&full_bar[kb], kStageBytes);
+        tma_load_2d(smem + kb * kStageBytes + kABytes, &tmB, &full_bar[kb], kb * BK, n0);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1u;
+        uint8_t* sa = smem + s * kStageBytes;
+        if (kb >= STAGES) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
+            enc_flag(FW_DEVERR_TIMEOUT);
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+          tma_load_2d(sa + kABytes, &tmB, &full_bar[s], kb * BK, n0);
+        }
+        if (kConv) {
+          const int k = kb * BK;
+          const int tap = k / conv_c;
+          const int c0 = k - tap * conv_c;
+          tma_load_3d(sa, &tmA, &full_bar[s], c0, tap % conv_stride, m0 + tap / conv_stride);
+        } else {
+          tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, m0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1u;
+        if (!mbar_wait(&full_bar[s], ph)) {
+          enc_flag(FW_DEVERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = base + s * kStageBytes;
+        const uint64_t adesc = sw128_desc(a_addr);
+        const uint64_t bdesc = sw128_desc(a_addr + kABytes);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          tc_mma_f16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+        tc_commit(&empty_bar[s]);
+      }
+      tc_commit(&tmem_bar);
+    }
+  } else {
+    pdl_wait();
+    const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to this warp
+    const int row = m0 + q * 32 + lane;
+    if (!mbar_wait(&tmem_bar, 0)) enc_flag(FW_DEVERR_TIMEOUT);
+    tc_fence_after();
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tc_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), r);
+      tc_wait_ld();
+      if (row < ep.M) epilogue_store16(ep, row, n0 + c, r);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Row LayerNorm: one warp per row, cols % 256 == 0 (<= 2048), two-pass variance in fp32.
+__global__ void __launch_bounds__(256) layernorm_rows_kernel(const half* __restrict__ x, const half* __restrict__ g,
+                                                             const half* __restrict__ b, half* __restrict__ y,
+                                                             int rows, int cols, float eps) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  const int nc = cols / 256;  // 16-byte chunks per lane
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * cols);
+  float v[64];
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c < nc) {
+      const uint4 u = xr[lane + 32 * c];
+      const half* hv = reinterpret_cast<const half*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[c * 8 + j] = __half2float(hv[j]);
+        sum += v[c * 8 + j];
+      }
+    }
+  }
+  sum = warp_sum(sum);
+  const float mean = sum / cols;
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    if (c < nc)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[c * 8 + j] - mean;
+        sq = fmaf(d, d, sq);
+      }
+  sq = warp_sum(sq);
+  const float inv = rsqrtf(sq / cols + eps);
+  uint4* yr = reinterpret_cast<uint4*>(y + static_cast<size_t>(row) * cols);
+  const uint4* g4 = reinterpret_cast<const uint4*>(g);
+  const uint4* b4 = reinterpret_cast<const uint4*>(b);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c < nc) {
+      const uint4 gu = __ldg(g4 + lane + 32 * c), bu = __ldg(b4 + lane + 32 * c);
+      const half* gh = reinterpret_cast<const half*>(&gu);
+      const half* bh = reinterpret_cast<const half*>(&bu);
+      uint4 out;
+      half* oh = reinterpret_cast<half*>(&out);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        oh[j] = __float2half(fmaf((v[c * 8 + j] - mean) * inv, __half2float(gh[j]), __half2float(bh[j])));
+      yr[lane + 32 * c] = out;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Encoder attention (mma.sync m16n8k16, fp16 in, fp32 accumulate/softmax).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// Byte offset of 16-byte chunk `c` of row `r` in a [rows x 64] fp16 tile with XOR swizzle.
+__device__ __forceinline__ uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+constexpr int kEncQ = 128;
+constexpr int kEncK = 64;
+
+__global__ void __launch_bounds__(256) enc_attention_kernel(const half* __restrict__ qkv, int64_t ld, int kcol,
+                                                            int vcol, half* __restrict__ out, int seq) {
+  __shared__ __align__(128) uint8_t qs[kEncQ * 128];
+  __shared__ __align__(128) uint8_t ks[2][kEncK * 128];
+  __shared__ __align__(128) uint8_t vs[2][kEncK * 128];
+  const int head = blockIdx.y;
+  const int q0 = blockIdx.x * kEncQ;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  pdl_trigger();
+
+  auto load_kv = [&](int kb, int buf) {
+    for (int i = threadIdx.x; i < kEncK * 8; i += 256) {
+      const int r = i >> 3, c = i & 7;
+      const int key = kb * kEncK + r;
+      const bool ok = key < seq;
+      const size_t rowoff = static_cast<size_t>(ok ? key : 0) * ld;
+      cp_async16(ks[buf] + swz(r, c), qkv + rowoff + kcol + head * 64 + c * 8, ok);
+      cp_async16(vs[buf] + swz(r, c), qkv + rowoff + vcol + head * 64 + c * 8, ok);
+    }
+  };
+  for (int i = threadIdx.x; i < kEncQ * 8; i += 256) {
+    const int r = i >> 3, c = i & 7;
+    const int qi = q0 + r;
+    const bool ok = qi < seq;
+    cp_async16(qs + swz(r, c), qkv + static_cast<size_t>(ok ? qi : 0) * ld + head * 64 + c * 8, ok);
+  }
+  load_kv(0, 0);
+  cp_async_commit();
+
+  const int nkb = (seq + kEncK - 1) / kEncK;
+  uint32_t qa[4][4];
+  float o[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY};
+  float lrow[2] = {0.f, 0.f};
+  constexpr float kLog2e = 1.4426950408889634f;
+  const uint32_t qs_base = smem_u32(qs);
+
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int buf = kb & 1;
+    if (kb + 1 < nkb) {
+      load_kv(kb + 1, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (kb == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int mi = lane >> 3, r = lane & 7;
+        const int row = warp * 16 + r + ((mi & 1) << 3);
+        const int chunk = 2 * kk + (mi >> 1);
+        ldsm_x4(qs_base + swz(row, chunk), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+      }
+    }
+    const uint32_t kbase = smem_u32(ks[buf]);
+    const uint32_t vbase = smem_u32(vs[buf]);
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const int mi = lane >> 3, r = lane & 7;
+        const int key = j * 8 + ((mi >> 1) << 3) + r;
+        const int chunk = 2 * kk + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + swz(key, chunk), b0, b1, b2, b3);
+        mma16816(s[j], qa[kk], b0, b1);
+        mma16816(s[j + 1], qa[kk], b2, b3);
+      }
+    }
+    // mask keys beyond the sequence, then the online softmax update
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int key = kb * kEncK + j * 8 + 2 * t;
+      if (key >= seq) s[j][0] = s[j][2] = -INFINITY;
+      if (key + 1 >= seq) s[j][1] = s[j][3] = -INFINITY;
+      mx[0] = fmaxf(mx[0], fmaxf(s[j][0], s[j][1]));
+      mx[1] = fmaxf(mx[1], fmaxf(s[j][2], s[j][3]));
+    }
+    float alpha[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+      const float mnew = fmaxf(mrow[i], mx[i]);
+      alpha[i] = exp2f((mrow[i] - mnew) * kLog2e);
+      mrow[i] = mnew;
+      lrow[i] *= alpha[i];
+    }
+    const float mb0 = mrow[0] * kLog2e, mb1 = mrow[1] * kLog2e;
+    uint32_t pa[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float p0 = exp2f(fmaf(s[j][0], kLog2e, -mb0));
+      const float p1 = exp2f(fmaf(s[j][1], kLog2e, -mb0));
+      const float p2 = exp2f(fmaf(s[j][2], kLog2e, -mb1));
+      const float p3 = exp2f(fmaf(s[j][3], kLog2e, -mb1));
+      lrow[0] += p0 + p1;
+      lrow[1] += p2 + p3;
+      pa[j >> 1][(j & 1) * 2 + 0] = pack_half2(p0, p1);
+      pa[j >> 1][(j & 1) * 2 + 1] = pack_half2(p2, p3);
+      o[j][0] *= alpha[0];
+      o[j][1] *= alpha[0];
+      o[j][2] *= alpha[1];
+      o[j][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int n = 0; n < 8; n += 2) {
+        const int mi = lane >> 3, r = lane & 7;
+        const int key = kk * 16 + ((mi & 1) << 3) + r;
+        const int chunk = n + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + swz(key, chunk), b0, b1, b2, b3);
+        mma16816(o[n], pa[kk], b0, b1);
+        mma16816(o[n + 1], pa[kk], b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 1);
+    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 2);
+  }
+  const float inv0 = 1.f / lrow[0], inv1 = 1.f / lrow[1];
+  const int r0 = q0 + warp * 16 + g;
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    const int col = head * 64 + n * 8 + 2 * t;
+    if (r0 < seq)
+      *reinterpret_cast<half2*>(out + static_cast<size_t>(r0) * (gridDim.y * 64) + col) =
+          __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
+    if (r0 + 8 < seq)
+      *reinterpret_cast<half2*>(out + static_cast<size_t>(r0 + 8) * (gridDim.y * 64) + col) =
+          __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D fp16 map [outer][inner] with row stride `ld` elements, box {64, box_outer}, 128B swizzle.
+static int make_map_2d(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                       uint32_t box_outer) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(FW_ERR_LAUNCH, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FW_ERR_ARG, "tensor map encode failed (%d)", static_cast<int>(r));
+  return FW_OK;
+}
+
+// 3-D fp16 map over a padded time-major conv input [rows][C] viewed as [rows/stride][stride][C],
+// box {64, 1, 128}.
+static int make_map_conv(CUtensorMap* m, const void* ptr, int C, int rows, int stride) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(FW_ERR_LAUNCH, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(stride),
+                        static_cast<cuuint64_t>(rows / stride)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(C) * 2 * stride};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FW_ERR_ARG, "conv tensor map encode failed (%d)", static_cast<int>(r));
+  return FW_OK;
+}
+
+template <int BN, int STAGES, bool kConv>
+static int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int K, int conv_c, int conv_stride,
+                         const GemmEpi& ep, cudaStream_t s, bool pdl) {
+  constexpr int smem = STAGES * (128 * 64 * 2 + BN * 64 * 2) + 1024;
+  auto kern = gemm_tc_kernel<BN, STAGES, kConv>;
+  cudaError_t e = ensure_smem(kern, smem);
+  if (e == cudaSuccess) {
+    dim3 grid((ep.M + 127) / 128, ep.N / BN);
+    e = launch(kern, grid, dim3(192), smem, s, pdl, ta, tb, K / 64, conv_c, conv_stride, ep);
+  }
+  return launch_status(e, "gemm_tc");
+}
+
+// Picks the N tile so that the grid covers the 148 SMs reasonably (M is 1500 or 3000 here).
+static int pick_bn(int M, int N) {
+  const int mt = (M + 127) / 128;
+  if (N % 256 == 0 && mt * (N / 256) >= 148) return 256;
+  if (N % 128 == 0 && mt * (N / 128) >= 148) return 128;
+  return 64;
+}
+
+static int gemm_dispatch(const CUtensorMap& ta, const void* B, int64_t ldb, int K, int conv_c, int conv_stride,
+                         bool conv, const GemmEpi& ep, cudaStream_t s, bool pdl) {
+  const int bn = pick_bn(ep.M, ep.N);
+  CUtensorMap tb;
+  int rc = make_map_2d(&tb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(ep.N), static_cast<uint64_t>(ldb), bn);
+  if (rc) return rc;
+  if (conv) {
+    if (bn == 256) return launch_gemm_t<256, 4, true>(ta, tb, K, conv_c, conv_stride, ep, s, pdl);
+    if (bn == 128) return launch_gemm_t<128, 3, true>(ta, tb, K, conv_c, conv_stride, ep, s, pdl);
+    return launch_gemm_t<64, 4, true>(ta, tb, K, conv_c, conv_stride, ep, s, pdl);
+  }
+  if (bn == 256) return launch_gemm_t<256, 4, false>(ta, tb, K, 0, 1, ep, s, pdl);
+  if (bn == 128) return launch_gemm_t<128, 3, false>(ta, tb, K, 0, 1, ep, s, pdl);
+  return launch_gemm_t<64, 4, false>(ta, tb, K, 0, 1, ep, s, pdl);
+}
+
+static int check_epi(const GemmEpi& ep, int K) {
+  FW_REQUIRE(ep.C != nullptr, FW_ERR_NULL, "gemm: C is required");
+  FW_REQUIRE(ep.M > 0 && ep.N > 0 && ep.N % 64 == 0 && K > 0 && K % 64 == 0, FW_ERR_SHAPE,
+             "gemm: need M > 0, N %% 64 == 0, K %% 64 == 0 (M=%d N=%d K=%d)", ep.M, ep.N, K);
+  FW_REQUIRE(ep.mode >= FW_EPI_BIAS && ep.mode <= FW_EPI_BIAS_SCALE, FW_ERR_ARG, "gemm: unknown epilogue %d", ep.mode);
+  FW_REQUIRE((ep.mode != FW_EPI_BIAS_RESID && ep.mode != FW_EPI_GELU_POS) || ep.R != nullptr, FW_ERR_NULL,
+             "gemm: this epilogue needs R");
+  FW_REQUIRE(ep.mode == FW_EPI_CROSS_KV || (ep.ldc >= ep.N && ep.ldc % 8 == 0), FW_ERR_SHAPE,
+             "gemm: ldc must be >= N and a multiple of 8");
+  FW_REQUIRE(aligned16(ep.C) && (ep.bias == nullptr || aligned16(ep.bias)) && (ep.R == nullptr || aligned16(ep.R)),
+             FW_ERR_ALIGN, "gemm: C, bias and R must be 16-byte aligned");
+  FW_REQUIRE(ep.R == nullptr || ep.ldr % 8 == 0, FW_ERR_ALIGN, "gemm: ldr must be a multiple of 8");
+  return FW_OK;
+}
+
+static int run_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int K, const GemmEpi& ep, cudaStream_t s,
+                    bool pdl) {
+  int rc = check_epi(ep, K);
+  if (rc) return rc;
+  FW_REQUIRE(A && B, FW_ERR_NULL, "gemm: A and B are required");
+  FW_REQUIRE(aligned16(A) && aligned16(B) && lda % 8 == 0 && ldb % 8 == 0 && lda >= K && ldb >= K, FW_ERR_ALIGN,
+             "gemm: A, B 16-byte aligned, lda/ldb >= K and multiples of 8");
+  CUtensorMap ta;
+  rc = make_map_2d(&ta, A, static_cast<uint64_t>(K), static_cast<uint64_t>(ep.M), static_cast<uint64_t>(lda), 128);
+  if (rc) return rc;
+  return gemm_dispatch(ta, B, ldb, K, 0, 1, false, ep, s, pdl);
+}
+
+static int run_conv(const void* X, int C, int rows_padded, int stride, const void* W, const GemmEpi& ep,
+                    cudaStream_t s, bool pdl) {
+  const int K = 3 * C;
+  int rc = check_epi(ep, K);
+  if (rc) return rc;
+  FW_REQUIRE(X && W, FW_ERR_NULL, "conv: X and W are required");
+  FW_REQUIRE(C % 64 == 0 && (stride == 1 || stride == 2) && rows_padded % stride == 0, FW_ERR_SHAPE,
+             "conv: C %% 64 == 0, stride 1 or 2, rows divisible by stride");
+  FW_REQUIRE(stride * (ep.M - 1) + 2 < rows_padded, FW_ERR_SHAPE, "conv: input too short for M output rows");
+  FW_REQUIRE(aligned16(X) && aligned16(W), FW_ERR_ALIGN, "conv: X and W must be 16-byte aligned");
+  CUtensorMap ta;
+  rc = make_map_conv(&ta, X, C, rows_padded, stride);
+  if (rc) return rc;
+  return gemm_dispatch(ta, W, K, K, C, stride, true, ep, s, pdl);
+}
+
+static int run_layernorm(const void* x, const void* g, const void* b, void* y, int rows, int cols, float eps,
+                         cudaStream_t s, bool pdl) {
+  FW_REQUIRE(x && g && b && y, FW_ERR_NULL, "layernorm_rows: all pointers are required");
+  FW_REQUIRE(rows > 0 && cols > 0 && cols % 256 == 0 && cols <= 2048, FW_ERR_SHAPE,
+             "layernorm_rows: cols must be a multiple of 256, <= 2048");
+  cudaError_t e = launch(layernorm_rows_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, pdl,
+                         static_cast<const half*>(x), static_cast<const half*>(g), static_cast<const half*>(b),
+                         static_cast<half*>(y), rows, cols, eps);
+  return launch_status(e, "layernorm_rows");
+}
+
+static int run_attention(const void* qkv, int64_t ld, int kcol, int vcol, void* out, int seq, int heads,
+                         cudaStream_t s, bool pdl) {
+  FW_REQUIRE(qkv && out, FW_ERR_NULL, "encoder_attention: qkv and out are required");
+  FW_REQUIRE(seq > 0 && heads > 0 && ld % 8 == 0 && kcol % 8 == 0 && vcol % 8 == 0, FW_ERR_SHAPE,
+             "encoder_attention: bad sizes");
+  FW_REQUIRE(aligned16(qkv) && aligned16(out), FW_ERR_ALIGN, "encoder_attention: 16-byte alignment required");
+  cudaError_t e = launch(enc_attention_kernel, dim3((seq + kEncQ - 1) / kEncQ, heads), dim3(256), 0, s, pdl,
+                         static_cast<const half*>(qkv), ld, kcol, vcol, static_cast<half*>(out), seq);
+  return launch_status(e, "encoder_attention");
+}
+
+unsigned int read_encoder_errors(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_fw_dev_error, sizeof(v));
+  if (clear) {
+    const unsigned int zero = 0;
+    cudaMemcpyToSymbol(g_fw_dev_error, &zero, sizeof(zero));
+  }
+  return v;
+}
+
+}  // namespace fw
+
+using namespace fw;
+
+extern "C" {
+
+int fw_gemm_f16(const void* A, int64_t lda, const void* B, int64_t ldb, const void* bias, void* C, int64_t ldc,
+                const void* R, int64_t ldr, int M, int N, int K, int epilogue, float scale, int scale_cols,
+                fw_stream_t stream) {
+  GemmEpi ep{static_cast<const half*>(bias), static_cast<half*>(C), ldc, static_cast<const half*>(R), ldr, M, N,
+             epilogue, scale, scale_cols};
+  return run_gemm(A, lda, B, ldb, K, ep, static_cast<cudaStream_t>(stream), false);
+}
+
+int fw_conv1d_k3_f16(const void* X, int C, int rows_padded, int stride, const void* W, const void* bias, void* Out,
+                     int64_t ldc, const void* R, int64_t ldr, int M, int N, int epilogue, fw_stream_t stream) {
+  GemmEpi ep{static_cast<const half*>(bias), static_cast<half*>(Out), ldc, static_cast<const half*>(R), ldr, M, N,
+             epilogue, 1.f, 0};
+  return run_conv(X, C, rows_padded, stride, W, ep, static_cast<cudaStream_t>(stream), false);
+}
+
+int fw_layernorm_rows(const void* x, const void* g, const void* b, void* y, int rows, int cols, float eps,
+                      fw_stream_t stream) {
+  return run_layernorm(x, g, b, y, rows, cols, eps, static_cast<cudaStream_t>(stream), false);
+}
+
+int fw_encoder_attention(const void* qkv, int64_t ld, int kcol, int vcol, void* out, int seq, int heads,
+                         fw_stream_t stream) {
+  return run_attention(qkv, ld, kcol, vcol, out, seq, heads, static_cast<cudaStream_t>(stream), false);
+}
+
+int fw_encoder_forward(const fw_encoder_t* e, fw_stream_t stream) {
+  FW_REQUIRE(e != nullptr, FW_ERR_NULL, "encoder_forward: descriptor is NULL");
+  FW_REQUIRE(e->n_layers >= 0 && e->n_layers <= FW_MAX_ENC_LAYERS && e->heads * 64 == kHidden &&
+                 e->n_frames == 2 * e->n_pos && e->n_dec_layers > 0,
+             FW_ERR_SHAPE, "encoder_forward: bad sizes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int T = e->n_pos, F = e->n_frames;
+  half* conv1_out = static_cast<half*>(e->conv1_out);
+  half* x = static_cast<half*>(e->x);
+  half* y = static_cast<half*>(e->y);
+  half* qkv = static_cast<half*>(e->qkv);
+  half* attn = static_cast<half*>(e->attn);
+  half* ffn = static_cast<half*>(e->ffn);
+  int rc;
+  // conv1 + GELU -> rows 1..F of conv1_out (rows 0 and F+1 stay zero)
+  GemmEpi ep{static_cast<const half*>(e->conv1_b), conv1_out + kHidden, kHidden, nullptr, 0, F, kHidden,
+             FW_EPI_BIAS_GELU, 1.f, 0};
+  if ((rc = run_conv(e->mel, 128, F + 2, 1, e->conv1_w, ep, s, true))) return rc;
+  // conv2 (stride 2) + GELU + sinusoid positions -> x
+  ep = GemmEpi{static_cast<const half*>(e->conv2_b), x, kHidden, static_cast<const half*>(e->pos), kHidden, T, kHidden,
+               FW_EPI_GELU_POS, 1.f, 0};
+  if ((rc = run_conv(conv1_out, kHidden, F + 2, 2, e->conv2_w, ep, s, true))) return rc;
+  for (int l = 0; l < e->n_layers; ++l) {
+    const fw_encoder_layer_t& L = e->layers[l];
+    if ((rc = run_layernorm(x, L.ln1_g, L.ln1_b, y, T, kHidden, e->eps, s, true))) return rc;
+    ep = GemmEpi{static_cast<const half*>(L.qkv_b), qkv, 3 * kHidden, nullptr, 0, T, 3 * kHidden,
+                 FW_EPI_BIAS_SCALE, 0.125f, kHidden};
+    if ((rc = run_gemm(y, kHidden, L.qkv_w, kHidden, kHidden, ep, s, true))) return rc;
+    if ((rc = run_attention(qkv, 3 * kHidden, kHidden, 2 * kHidden, attn, T, e->heads, s, true))) return rc;
+    ep = GemmEpi{static_cast<const half*>(L.out_b), x, kHidden, x, kHidden, T, kHidden, FW_EPI_BIAS_RESID, 1.f, 0};
+    if ((rc = run_gemm(attn, kHidden, L.out_w, kHidden, kHidden, ep, s, true))) return rc;
+    if ((rc = run_layernorm(x, L.ln2_g, L.ln2_b, y, T, kHidden, e->eps, s, true))) return rc;
+    ep = GemmEpi{static_cast<const half*>(L.fc1_b), ffn, kFfn, nullptr, 0, T, kFfn, FW_EPI_BIAS_GELU, 1.f, 0};
+    if ((rc = run_gemm(y, kHidden, L.fc1_w, kHidden, kHidden, ep, s, true))) return rc;
+    ep = GemmEpi{static_cast<const half*>(L.fc2_b), x, kHidden, x, kHidden, T, kHidden, FW_EPI_BIAS_RESID, 1.f, 0};
+    if ((rc = run_gemm(ffn, kFfn, L.fc2_w, kFfn, kFfn, ep, s, true))) return rc;
+  }
+  if ((rc = run_layernorm(x, e->final_g, e->final_b, e->enc_out, T, kHidden, e->eps, s, true))) return rc;
+  const int ncross = e->n_dec_layers * 2 * kHidden;
+  ep = GemmEpi{static_cast<const half*>(e->cross_b), static_cast<half*>(e->cross_kv), 0, nullptr, 0, T, ncross,
+               FW_EPI_CROSS_KV, 1.f, 0};
+  return run_gemm(e->enc_out, kHidden, e->cross_w, kHidden, kHidden, ep, s, true);
+}
+
+}  // extern "C"

@@ -1,0 +1,235 @@
+/*
+ * flash_whisper_b200 — C ABI of the B200 (sm_100a) kernels for batch-1 Whisper-large-v3-turbo.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream, launches asynchronously
+ * on that stream, allocates nothing, and returns an int status (FW_OK = 0). On a non-zero status
+ * fw_last_error_string() holds a one-line message for the calling thread. No entry point
+ * synchronises the host, so all of them can be recorded into a CUDA graph.
+ *
+ * The first four entry points replace the reference's pybind kernels one for one
+ * (custom/kernels/whisper_kernels.cu:278-363, bound by custom/ext.py:13-18); the Python wrapper in
+ * flash_whisper_b200/ext.py keeps their argument order and error behaviour. The rest are the fused
+ * decode path, the GPU log-mel front end and the tcgen05 encoder that replace the torch / cuBLAS /
+ * cuFFT / HF-transformers calls made by custom/model.py.
+ *
+ * fp16 tensors are passed as `void*` (IEEE binary16), row-major, contiguous.
+ */
+#ifndef FLASH_WHISPER_H_
+#define FLASH_WHISPER_H_
+
+#include <stdbool.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* fw_stream_t; /* a cudaStream_t; NULL means the legacy default stream */
+
+enum {
+  FW_OK = 0,
+  FW_ERR_NULL = 1,        /* a required pointer is NULL */
+  FW_ERR_SHAPE = 2,       /* a size argument is out of range or inconsistent */
+  FW_ERR_ALIGN = 3,       /* a pointer or stride is not aligned as the kernel requires */
+  FW_ERR_ARG = 4,         /* optional arguments given inconsistently */
+  FW_ERR_LAUNCH = 5,      /* the CUDA launch failed */
+  FW_ERR_UNSUPPORTED = 6  /* the current device is not an sm_100 part */
+};
+
+/* Bits of the device-side error word (fw_device_error). */
+#define FW_DEVERR_TIMEOUT 1u    /* a bounded wait inside a kernel gave up */
+#define FW_DEVERR_BAD_INDEX 2u  /* a token id / position read from device memory was out of range */
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* fw_last_error_string(void);
+/* ABI version of this library. */
+int fw_version(void);
+/* Reads (and optionally clears) the OR of every kernel's device error bits. Synchronises. */
+int fw_device_error(unsigned int* bits, int clear);
+
+/* ------------------------------------------------------------------------------------------
+ * Reference kernel surface
+ * ---------------------------------------------------------------------------------------- */
+
+/* h <- fp16(h + x) when x != NULL, then y = LayerNorm(h) * gamma + beta (fp32 math, two-pass
+ * variance). hidden must be 1280.
+ * Replaces add_layernorm, custom/kernels/whisper_kernels.cu:341-356 (kernel :217-267). */
+int fw_add_layernorm(void* h, const void* x, const void* gamma, const void* beta, void* y, int hidden, float eps,
+                     fw_stream_t stream);
+
+/* Single-query split-K attention over k/v [heads, max_len, 64]. Self attention: len_state, k_new
+ * and v_new are all given; the attended length is len_state[0] + 1 read on the device, and the row
+ * at len_state[0] of k/v is overwritten with k_new/v_new [heads, 64]. Cross attention: all three
+ * NULL, length = max_len. part_* are fp32 scratch of at least heads*splits (m, l) and
+ * heads*splits*64 (acc) elements, splits = ceil(max_len / 64); their sizes are passed so the call
+ * can reject a workspace that is too small. out is fp16 [heads*64].
+ * Replaces decode_attention, custom/kernels/whisper_kernels.cu:300-339 (kernels :108-213). */
+int fw_decode_attention(const void* q, void* k, void* v, void* out, const int64_t* len_state, const void* k_new,
+                        const void* v_new, float* part_m, int64_t part_m_numel, float* part_l, int64_t part_l_numel,
+                        float* part_acc, int64_t part_acc_numel, int heads, int max_len, float scale,
+                        fw_stream_t stream);
+
+/* best <- max(best, key of argmax_{r, !suppress[r]} fp16(w[r] . h)) with the packed
+ * (score, ~index) u64 key, so ties go to the lower index. best must hold 0 on entry.
+ * Replaces lm_head_argmax, custom/kernels/whisper_kernels.cu:278-289 (kernel :30-86). */
+int fw_lm_head_argmax(const void* h, const void* w, const bool* suppress, int vocab, int hidden, int64_t* best,
+                      fw_stream_t stream);
+
+/* Decodes best into a token, appends it to tokens[state[1]] (when state[1] < max_pos and
+ * < n_tokens), feeds it back into cur, advances state[0] (capped at max_pos-1) and resets best.
+ * Replaces argmax_finalize, custom/kernels/whisper_kernels.cu:291-298 (kernel :90-100). */
+int fw_argmax_finalize(int64_t* best, int64_t* tokens, int64_t n_tokens, int64_t* state, int64_t* cur, int max_pos,
+                       fw_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Stand-alone decode ops (the torch calls of custom/model.py:110,120 and the argmax microbench)
+ * ---------------------------------------------------------------------------------------- */
+
+/* out[i] = fp16(embed[ids[i]] + pos_embed[positions[i]]), i < n; rows of `hidden` fp16.
+ * Replaces the index_select + add of custom/model.py:110. */
+int fw_embed_pos(const void* embed, const void* pos_embed, const int64_t* ids, const int64_t* positions, void* out,
+                 int n, int vocab, int max_pos, int hidden, fw_stream_t stream);
+
+/* y = fp16(gelu_erf(x)), n elements. Replaces F.gelu of custom/model.py:120. */
+int fw_gelu(const void* x, void* y, int64_t n, fw_stream_t stream);
+
+/* out_index[0] = argmax over i < n with !suppress[i] (suppress may be NULL) of fp16 logits,
+ * first index on ties (torch.argmax). key is an int64 scratch word that must hold 0 on entry and is
+ * left at 0. */
+int fw_argmax_f16(const void* logits, int64_t n, const bool* suppress, int64_t* key, int64_t* out_index,
+                  fw_stream_t stream);
+
+/* out[r] = epilogue(W[r] . LN(h) + b[r]) for r < n_out, LN over hidden=1280 with gamma/beta/eps.
+ * act 0: fp16(acc + b); act 1: fp16(gelu(fp16(acc + b))). b may be NULL.
+ * Fuses add_layernorm (custom/model.py:113,116,119) with the F.linear that follows it
+ * (custom/model.py:114,117,120). */
+int fw_ln_gemv(const void* h, const void* gamma, const void* beta, float eps, const void* w, const void* b,
+               void* out, int n_out, int hidden, int act, fw_stream_t stream);
+
+/* h[r] = fp16(h[r] + fp16(W[r] . x + b[r])) for r < n_out; x has k elements (k % 256 == 0).
+ * Fuses F.linear (custom/model.py:116,119,120) with the residual add of the next add_layernorm. */
+int fw_gemv_residual(const void* x, int k, const void* w, const void* b, void* h, int n_out, fw_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Whole decode step (custom/model.py:107-123) as 34 PDL-chained launches.
+ * ---------------------------------------------------------------------------------------- */
+#define FW_MAX_LAYERS 8
+
+typedef struct {
+  const void *ln1_g, *ln1_b, *ln2_g, *ln2_b, *ln3_g, *ln3_b; /* [1280] */
+  const void *qkv_w, *qkv_b;                                 /* [3840,1280], [3840] (K bias zero) */
+  const void *out_w, *out_b;                                 /* [1280,1280], [1280] */
+  const void *cq_w, *cq_b;                                   /* cross q_proj */
+  const void *co_w, *co_b;                                   /* cross out_proj */
+  const void *fc1_w, *fc1_b;                                 /* [5120,1280], [5120] */
+  const void *fc2_w, *fc2_b;                                 /* [1280,5120], [1280] */
+  void *self_k, *self_v;                                     /* [heads, max_pos, 64] */
+  const void *cross_k, *cross_v;                             /* [heads, enc_len, 64] */
+} fw_decoder_layer_t;
+
+typedef struct {
+  int n_layers, heads, max_pos, enc_len, vocab, prompt_len;
+  float eps, scale;
+  const void *embed, *pos_embed, *lm_head; /* [vocab,1280], [max_pos,1280], [vocab,1280] */
+  const void *final_g, *final_b;           /* [1280] */
+  const bool *base_mask, *first_mask;      /* [vocab]; first_mask applies to the last prompt step */
+  const int64_t* prompt;                   /* [prompt_len] forced input ids (may be NULL if 0) */
+  fw_decoder_layer_t layers[FW_MAX_LAYERS];
+  void *h, *qkv, *attn, *cq, *ffn;          /* fp16 [1280], [3840], [1280], [1280], [5120] */
+  float *part_m, *part_l, *part_acc;        /* attention split scratch */
+  int64_t ws_splits;                        /* capacity of part_m/part_l in splits per head */
+  unsigned int* counters;                   /* [heads + 1], zero before the first step; left zero */
+  int64_t *cur, *state, *tokens, *best;     /* [1], [2] = {position, count}, [n_tokens], [1] (0) */
+  int64_t n_tokens;
+} fw_decoder_t;
+
+/* Launches `steps` decode steps. Step semantics follow custom/model.py:107-123 and :197-207:
+ * while state[0] < prompt_len - 1 the input id is prompt[state[0]] and the prediction is
+ * discarded; at state[0] == prompt_len - 1 first_mask applies and the prediction becomes tokens[0];
+ * afterwards base_mask applies and each prediction is appended and fed back. */
+int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * GPU log-mel front end (custom/model.py:93-98; WhisperFeatureExtractor semantics)
+ * ---------------------------------------------------------------------------------------- */
+
+/* wave fp32 [batch, n_samples]; filters fp32 [201, 128] (Slaney mel filterbank, n_fft 400);
+ * scratch fp32 [batch, 128, n_frames] and clip_max u32 [batch] are caller-owned scratch;
+ * n_frames = n_samples / 160. Output fp16: layout 0 = [batch, 128, n_frames] (as the reference's
+ * mel buffer), layout 1 = [batch, n_frames + 2, 128] time-major with one zero row on each side
+ * (the encoder's conv1 operand). */
+int fw_log_mel(const float* wave, int batch, int n_samples, const float* filters, float* scratch,
+               unsigned int* clip_max, void* mel_out, int layout, fw_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Encoder (HF WhisperEncoder as called by custom/model.py:143-147)
+ * ---------------------------------------------------------------------------------------- */
+
+/* Epilogues of fw_gemm_f16 (acc is the fp32 tensor-core accumulator). */
+#define FW_EPI_BIAS 0         /* C = fp16(acc + bias) */
+#define FW_EPI_BIAS_GELU 1    /* C = fp16(gelu(fp16(acc + bias))) */
+#define FW_EPI_BIAS_RESID 2   /* C = fp16(R + fp16(acc + bias)); R may alias C */
+#define FW_EPI_GELU_POS 3     /* C = fp16(fp16(gelu(fp16(acc + bias))) + R[row]) (conv2 + positions) */
+#define FW_EPI_CROSS_KV 4     /* cross K/V scatter into [layers, 2, heads, M, 64] */
+#define FW_EPI_BIAS_SCALE 5   /* C = fp16(fp16(acc + bias) * scale) for columns < scale_cols */
+
+/* C[M, N] = epilogue(A[M, K] . B[N, K]^T + bias[N]) on tcgen05 tensor cores, fp16 in, fp32
+ * accumulate in TMEM. lda/ldb/ldc/ldr are row strides in elements. K % 64 == 0, N % 64 == 0;
+ * lda, ldb >= K and multiples of 8; A, B, C, bias, R 16-byte aligned. bias may be NULL.
+ * FW_EPI_CROSS_KV writes column n of row m to C[((n / 64) * M + m) * 64 + n % 64], i.e. the
+ * [layers, 2, heads, M, 64] cross-attention cache of custom/model.py:146 (ldc ignored).
+ * Replaces the torch/cuBLAS GEMMs of the HF encoder and custom/model.py:145. */
+int fw_gemm_f16(const void* A, int64_t lda, const void* B, int64_t ldb, const void* bias, void* C, int64_t ldc,
+                const void* R, int64_t ldr, int M, int N, int K, int epilogue, float scale, int scale_cols,
+                fw_stream_t stream);
+
+/* Conv1d(kernel 3, padding 1, stride 1 or 2) as an implicit GEMM on the same tensor cores.
+ * X is the time-major input [rows_padded, C] whose first and last rows are zero padding;
+ * W is [N, 3*C] ordered (tap, channel), i.e. torch's [N, C, 3] weight permuted to [N, 3, C].
+ * Output row t (t < M) = epilogue(sum_j X[stride*t + j] . W[:, j*C:(j+1)*C]^T + bias).
+ * Replaces conv1/conv2 of the HF WhisperEncoder. */
+int fw_conv1d_k3_f16(const void* X, int C, int rows_padded, int stride, const void* W, const void* bias, void* Out,
+                     int64_t ldc, const void* R, int64_t ldr, int M, int N, int epilogue, fw_stream_t stream);
+
+/* Row-wise LayerNorm: y[r] = LN(x[r]) * g + b, rows x cols fp16 (cols % 256 == 0). */
+int fw_layernorm_rows(const void* x, const void* g, const void* b, void* y, int rows, int cols, float eps,
+                      fw_stream_t stream);
+
+/* Bidirectional multi-head attention for the encoder. qkv fp16 [seq, ld] holding pre-scaled q at
+ * column h*64, k at kcol + h*64 and v at vcol + h*64; out fp16 [seq, heads*64]. */
+int fw_encoder_attention(const void* qkv, int64_t ld, int kcol, int vcol, void* out, int seq, int heads,
+                         fw_stream_t stream);
+
+#define FW_MAX_ENC_LAYERS 32
+typedef struct {
+  const void *ln1_g, *ln1_b, *ln2_g, *ln2_b;
+  const void *qkv_w, *qkv_b; /* [3840,1280] = q_proj, k_proj, v_proj; bias (k part zero) */
+  const void *out_w, *out_b;
+  const void *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+} fw_encoder_layer_t;
+
+typedef struct {
+  int n_layers, n_frames, n_pos, n_dec_layers, heads;
+  float eps;
+  const void* mel;                 /* fp16 [n_frames + 2, 128] time-major, zero rows at both ends */
+  const void *conv1_w, *conv1_b;   /* [1280, 3*128] ordered (tap, channel); [1280] */
+  const void *conv2_w, *conv2_b;   /* [1280, 3*1280] ordered (tap, channel); [1280] */
+  const void* pos;                 /* [n_pos, 1280] sinusoid table */
+  fw_encoder_layer_t layers[FW_MAX_ENC_LAYERS];
+  const void *final_g, *final_b;
+  const void *cross_w, *cross_b;   /* [n_dec_layers*2*1280, 1280], bias (K parts zero) */
+  void* conv1_out;                 /* fp16 [n_frames + 2, 1280], rows 0 and n_frames+1 zero */
+  void *x, *y, *qkv, *attn, *ffn;  /* fp16 [n_pos,1280], [n_pos,1280], [n_pos,3840], [n_pos,1280],
+                                      [n_pos,5120] */
+  void* enc_out;                   /* fp16 [n_pos, 1280] final-LN output */
+  void* cross_kv;                  /* fp16 [n_dec_layers, 2, heads, n_pos, 64] */
+} fw_encoder_t;
+
+/* mel -> encoder states -> cross K/V for every decoder layer (custom/model.py:143-147). */
+int fw_encoder_forward(const fw_encoder_t* e, fw_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_WHISPER_H_ */

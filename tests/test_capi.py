@@ -1,0 +1,65 @@
+"""CPU tests of the C-ABI boundary: the library loads, exports everything the header declares, and
+rejects bad arguments with the reference's error messages before touching a GPU."""
+
+import ctypes
+
+import pytest
+import torch
+
+from flash_whisper_b200 import _lib
+from flash_whisper_b200.ext import Ext
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    declared = _lib.header_symbols()
+    assert len(declared) >= 19
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+    assert set(declared) == set(_lib._SIGNATURES)
+    assert lib.fw_version() == 1
+
+
+def test_null_pointers_return_status_and_message():
+    lib = _lib.lib()
+    rc = lib.fw_add_layernorm(None, None, None, None, None, 1280, 1e-5, None)
+    assert rc == 1  # FW_ERR_NULL
+    assert b'required' in lib.fw_last_error_string()
+    p = ctypes.c_void_p(16)
+    rc = lib.fw_add_layernorm(p, None, p, p, p, 1024, 1e-5, None)
+    assert rc == 2 and b'hidden size must be 1280' in lib.fw_last_error_string()
+    rc = lib.fw_decode_attention(p, p, p, p, None, p, None, p, 100, p, 100, p, 6400, 20, 448, 0.125, None)
+    assert rc == 4 and b'given together' in lib.fw_last_error_string()
+    rc = lib.fw_decode_attention(p, p, p, p, None, None, None, p, 10, p, 10, p, 640, 20, 448, 0.125, None)
+    assert rc == 2 and b'workspace too small for 7 splits' in lib.fw_last_error_string()
+    rc = lib.fw_gemm_f16(p, 64, p, 64, None, p, 64, None, 0, 100, 60, 64, 0, 1.0, 0, None)
+    assert rc == 2
+    rc = lib.fw_log_mel(p, 1, 1000, p, p, p, p, 0, None)
+    assert rc == 2
+
+
+def test_decoder_struct_matches_header_layout():
+    # offsets the C struct would have: ints, floats, pointers in declaration order (x86-64 LP64)
+    assert ctypes.sizeof(_lib.DecoderLayer) == 22 * 8
+    assert _lib.Decoder.layers.offset == 8 * 4 + 8 * 8
+    assert ctypes.sizeof(_lib.EncoderLayer) == 12 * 8
+
+
+def test_wrapper_checks_mirror_reference_messages():
+    ext = Ext()
+    h = torch.zeros(1280, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match='h must be contiguous CUDA fp16'):
+        ext.add_layernorm(h, None, h, h, h, 1e-5)
+    with pytest.raises(RuntimeError, match='q must be contiguous CUDA fp16'):
+        ext.decode_attention(h, h, h, h, None, None, None, h, h, h, 0.125)
+    with pytest.raises(RuntimeError, match='tokens, state and cur must be int64'):
+        ext.argmax_finalize(torch.zeros(1, dtype=torch.long), torch.zeros(4, dtype=torch.int32),
+                            torch.zeros(2, dtype=torch.long), torch.zeros(1, dtype=torch.long), 448)
+
+
+def test_model_requires_cuda_without_fallback():
+    if torch.cuda.is_available():
+        pytest.skip('CUDA present')
+    from flash_whisper_b200.model import CustomModel
+    with pytest.raises(RuntimeError, match='requires a CUDA device'):
+        CustomModel()
