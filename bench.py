@@ -168,6 +168,7 @@ def bench_reference(args, rank, world):
     return 0
 
 
+@torch.inference_mode()
 def bench_ours(args, rank, world, local_rank):
     from flash_whisper_b200.audio import synthetic_audio
     from flash_whisper_b200.model import CustomModel
@@ -177,7 +178,8 @@ def bench_ours(args, rank, world, local_rank):
     dims = TURBO
     model = CustomModel(state_dict=random_state_dict(0, dims), dims=dims, selftest=False)
     audio = synthetic_audio(rank, SECONDS)
-    model.wave.copy_(torch.from_numpy(audio))
+    model.load_audio(audio)
+    torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
 
     def barrier():

@@ -247,6 +247,15 @@ class CustomModel:
     def run_chunk(self):
         self.graph_chunk.replay() if self.graph_chunk else self._chunk()
 
+    @torch.inference_mode()
+    def load_audio(self, audio):
+        """Copies a host clip (zero-padded to 30 s) into the device waveform buffer."""
+        host = self.wave_host.numpy()
+        host[:audio.size] = audio
+        host[audio.size:] = 0.0
+        self.wave.copy_(self.wave_host, non_blocking=True)
+
+    @torch.inference_mode()
     def decode_device(self, n_tokens):
         """Device-resident pipeline after the waveform is in self.wave: front, prompt, chunks."""
         self.run_front()

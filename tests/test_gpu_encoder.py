@@ -12,9 +12,15 @@ from flash_whisper_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-def _close(out, ref, rtol=1e-2, atol=1e-3):
+def _close(out, ref, rtol=1e-2, atol=1e-3, inner=None):
+    """|out - ref| <= atol + rtol |ref| (+ one fp16 ulp of `inner`, the fp16-rounded accumulator an
+    epilogue rounds before adding a residual or applying GELU: a different fp32 summation order may
+    round it one ulp apart, and that ulp survives cancellation in the sum)."""
     out, ref = out.float(), ref.float()
-    bad = (out - ref).abs() > atol + rtol * ref.abs()
+    tol = atol + rtol * ref.abs()
+    if inner is not None:
+        tol = tol + inner.float().abs() * 2.0 ** -10
+    bad = (out - ref).abs() > tol
     assert not bool(bad.any()), (f'{int(bad.sum())} / {bad.numel()} mismatches, max abs diff '
                                  f'{float((out - ref).abs().max())}')
 
@@ -42,14 +48,14 @@ def test_gemm_epilogues(ext):
     acc = (a.float() @ b.float().T + bias.float()).half().float()
     c = torch.empty(m, n, device='cuda', dtype=torch.float16)
     ext.gemm(a, b, bias, c, _lib.FW_EPI_BIAS_GELU)
-    _close(c, F.gelu(acc).half())
+    _close(c, F.gelu(acc).half(), inner=acc)
     r = _rand(m, n, seed=7)
     c = r.clone()
     ext.gemm(a, b, bias, c, _lib.FW_EPI_BIAS_RESID, r=c)  # in place, as the encoder residual does
-    _close(c, (r.float() + acc).half())
+    _close(c, (r.float() + acc).half(), inner=acc)
     pos = _rand(m, n, seed=8)
     ext.gemm(a, b, bias, c, _lib.FW_EPI_GELU_POS, r=pos)
-    _close(c, (F.gelu(acc).half().float() + pos.float()).half())
+    _close(c, (F.gelu(acc).half().float() + pos.float()).half(), inner=acc)
     ext.gemm(a, b, bias, c, _lib.FW_EPI_BIAS_SCALE, scale=0.125, scale_cols=640)
     ref = acc.clone()
     ref[:, :640] *= 0.125
@@ -112,9 +118,10 @@ def test_encoder_forward_vs_numpy_oracle(ext):
     sd = random_state_dict(5, dims, bias_std=0.02, ln_std=0.05)
     model = CustomModel(state_dict=sd, dims=dims, selftest=False, capture=False)
     wave = pad_to_30s(synthetic_audio(3, 30.0))
-    model.wave.copy_(torch.from_numpy(wave))
-    model._mel()
-    model._encode()
+    model.load_audio(wave)
+    with torch.inference_mode():
+        model._mel()
+        model._encode()
     torch.cuda.synchronize()
     o = WhisperOracle(sd, dims)
     mel16 = model.mel[1:-1].float().cpu().numpy().T
