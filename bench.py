@@ -38,6 +38,9 @@ sys.path.insert(0, str(ROOT))
 SECONDS = 30.0
 N_TOKENS = 224
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
+# dram__bytes_read.sum + dram__bytes_write.sum of one lm_head_kernel launch (ncu --set full on the
+# selftest case, W 51866 x 1280 fp16): 132.84 MB read + 3.68 MB written.
+LM_HEAD_TRAFFIC_BYTES = 132_841_472 + 3_681_792
 
 
 def peaks():
@@ -284,7 +287,7 @@ def bench_ours(args, rank, world, local_rank):
         'throughput_audio_s_per_s': round(world * SECONDS / (step_ms / 1e3), 2),
         'roofline': {'bound': 'hbm', 'kernel': 'lm_head_argmax (GEMV 51866x1280 + argmax)',
                      'achieved': round(lm_gbs, 1), 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
-                     'frac': round(lm_gbs / pk['hbm_gbs'], 4), 'traffic': None, 'peak_source': pk['source'],
+                     'frac': round(lm_gbs / pk['hbm_gbs'], 4), 'traffic': LM_HEAD_TRAFFIC_BYTES, 'peak_source': pk['source'],
                      'launch_us': round(lm_us, 3), 'bytes_per_launch': lm_bytes},
         'roofline_decode_step': {'bound': 'hbm', 'achieved': round(dec_gbs, 1), 'peak': pk['hbm_gbs'],
                                  'unit': 'GB/s', 'frac': round(dec_gbs / pk['hbm_gbs'], 4),
