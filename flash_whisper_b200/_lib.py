@@ -66,6 +66,7 @@ _SIGNATURES = {
     'fw_add_layernorm': (c_int, [vp, vp, vp, vp, vp, c_int, c_float, vp]),
     'fw_decode_attention': (c_int, [vp, vp, vp, vp, vp, vp, vp, vp, c_int64, vp, c_int64, vp, c_int64, c_int, c_int,
                                     c_float, vp]),
+    'fw_decode_attention_noalloc': (c_int, [vp, vp, vp, vp, vp, vp, vp, c_int, c_int, c_float, vp]),
     'fw_lm_head_argmax': (c_int, [vp, vp, vp, c_int, c_int, vp, vp]),
     'fw_argmax_finalize': (c_int, [vp, vp, c_int64, vp, vp, c_int, vp]),
     'fw_embed_pos': (c_int, [vp, vp, vp, vp, vp, c_int, c_int, c_int, c_int, vp]),

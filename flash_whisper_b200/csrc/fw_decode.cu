@@ -16,6 +16,8 @@
 // kernel N overlaps the tail of kernel N-1. Dot products use the same per-lane order and warp
 // xor-tree as the reference kernels so that the LM-head logits, LayerNorm outputs and attention
 // outputs are bit-identical to the reference kernels given identical inputs.
+#include <mutex>
+
 #include "fw_common.cuh"
 #include "fw_host.h"
 
@@ -730,6 +732,43 @@ static int launch_lm_head(LmParams p, cudaStream_t s, bool pdl) {
   return launch_status(e, "lm_head_argmax");
 }
 
+// ---------------------------------------------------------------------------------------------
+// Split-K attention without caller-allocated workspace (fw_decode_attention_noalloc).
+// The fp32 split partials live in this fixed device array instead: per GPU that loads the library,
+// kNoAllocMaxSlots head-splits x (64 accumulators + max + sum) x 4 bytes = 528 KB, held until the
+// process exits. Host code must not hand the symbol itself to a kernel (on the host it only names
+// a stand-in); its device address is looked up once per device with cudaGetSymbolAddress.
+constexpr int kNoAllocMaxSlots = 2048;  // heads * ceil(max_len / 64)
+static __device__ __align__(256) float g_attn_noalloc_scratch[kNoAllocMaxSlots * (kHeadDim + 2)];
+
+// Device address of g_attn_noalloc_scratch on the current device; looked up on the first call per
+// device and cached. Returns nullptr and sets the error message on failure.
+static float* noalloc_scratch() {
+  static std::mutex mu;
+  static float* cached[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error(FW_ERR_LAUNCH, "decode_attention_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    set_error(FW_ERR_UNSUPPORTED, "decode_attention_noalloc: device index %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error(FW_ERR_LAUNCH, "decode_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    cached[dev] = static_cast<float*>(p);
+  }
+  return cached[dev];
+}
+
 unsigned int read_decode_errors(bool clear) {
   unsigned int v = 0;
   cudaMemcpyFromSymbol(&v, g_fw_dev_error, sizeof(v));
@@ -780,6 +819,36 @@ int fw_decode_attention(const void* q, void* k, void* v, void* out, const int64_
                          static_cast<const float*>(part_m), static_cast<const float*>(part_l),
                          static_cast<const float*>(part_acc), static_cast<half*>(out), splits);
   return launch_status(e, "decode_attention_combine");
+}
+
+int fw_decode_attention_noalloc(const void* q, void* k, void* v, void* out, const int64_t* len_state,
+                                const void* k_new, const void* v_new, int heads, int max_len, float scale,
+                                fw_stream_t stream) {
+  FW_REQUIRE(q && k && v && out, FW_ERR_NULL, "decode_attention_noalloc: q, k, v and out are required");
+  FW_REQUIRE((k_new != nullptr) == (v_new != nullptr) && (k_new != nullptr) == (len_state != nullptr), FW_ERR_ARG,
+             "len_state, k_new and v_new must be given together");
+  FW_REQUIRE(heads > 0 && max_len > 0, FW_ERR_SHAPE, "k, v must be [heads, max_len, 64]");
+  const int splits = (max_len + kSplitKeys - 1) / kSplitKeys;
+  FW_REQUIRE(int64_t(heads) * splits <= kNoAllocMaxSlots, FW_ERR_SHAPE,
+             "decode_attention_noalloc: heads * ceil(max_len / 64) = %lld exceeds the fixed scratch of %d "
+             "head-splits; use fw_decode_attention with a caller workspace",
+             static_cast<long long>(int64_t(heads) * splits), kNoAllocMaxSlots);
+  FW_REQUIRE(aligned16(k) && aligned16(v), FW_ERR_ALIGN, "k and v must be 16-byte aligned");
+  float* scratch = noalloc_scratch();
+  if (scratch == nullptr) return FW_ERR_LAUNCH;
+  float* part_acc = scratch;
+  float* part_m = scratch + kNoAllocMaxSlots * kHeadDim;
+  float* part_l = part_m + kNoAllocMaxSlots;
+  AttnParams p{static_cast<const half*>(q), static_cast<half*>(k), static_cast<half*>(v),
+               static_cast<const half*>(k_new), static_cast<const half*>(v_new), len_state, max_len, scale,
+               part_m, part_l, part_acc, static_cast<half*>(out), nullptr};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = launch_attention(p, heads, splits, s, false);
+  if (rc) return rc;
+  cudaError_t e = launch(attn_combine_kernel, dim3(heads), dim3(kHeadDim), 0, s, false,
+                         static_cast<const float*>(part_m), static_cast<const float*>(part_l),
+                         static_cast<const float*>(part_acc), static_cast<half*>(out), splits);
+  return launch_status(e, "decode_attention_noalloc_combine");
 }
 
 int fw_lm_head_argmax(const void* h, const void* w, const bool* suppress, int vocab, int hidden, int64_t* best,

@@ -69,6 +69,23 @@ int fw_decode_attention(const void* q, void* k, void* v, void* out, const int64_
                         float* part_acc, int64_t part_acc_numel, int heads, int max_len, float scale,
                         fw_stream_t stream);
 
+/* fw_decode_attention for callers that cannot allocate device memory. No counterpart in the
+ * reference. Some callers cannot call cudaMalloc: a host that is recording a CUDA graph (allocation
+ * is not allowed while capture is in progress), a plug-in whose device memory belongs to the host
+ * application's allocator or a fixed budget, or a real-time audio thread that must not block on
+ * the implicit device synchronisation cudaMalloc / cudaFree can cause. This variant takes no
+ * workspace: its split partials live in one fixed device array compiled into the library
+ * (528 KB on every GPU that loads it, held until the process exits), so it accepts at most
+ * heads * ceil(max_len / 64) <= 2048 head-splits and returns FW_ERR_SHAPE beyond that.
+ * Semantics, arguments and results are otherwise those of fw_decode_attention. The first call on
+ * each device looks up the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture. All calls share the one array and nothing in it
+ * needs to start at zero (every split slot is written before the combine reads it), but calls
+ * that overlap on the GPU (e.g. on two streams) race on it and must be serialised. */
+int fw_decode_attention_noalloc(const void* q, void* k, void* v, void* out, const int64_t* len_state,
+                                const void* k_new, const void* v_new, int heads, int max_len, float scale,
+                                fw_stream_t stream);
+
 /* best <- max(best, key of argmax_{r, !suppress[r]} fp16(w[r] . h)) with the packed
  * (score, ~index) u64 key, so ties go to the lower index. best must hold 0 on entry.
  * Replaces lm_head_argmax, custom/kernels/whisper_kernels.cu:278-289 (kernel :30-86). */
