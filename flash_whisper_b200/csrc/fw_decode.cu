@@ -152,17 +152,36 @@ struct AttnParams {
   unsigned int* counters;
 };
 
+constexpr int kMaxSplits = 128;  // max_len <= 8192 keys
+
+// Merges the splits of one head (the combine of whisper_kernels.cu:193-213, same operation order so
+// the result is bit-identical). The split maxima and sums are first staged in shared memory by the
+// whole CTA, and the per-split accumulators are loaded 16 at a time, so the merge costs two rounds of
+// L2 latency instead of one round per split. Call with all threads of the CTA; threads < 64 write.
 __device__ __forceinline__ void combine_head(const float* pm, const float* pl, const float* pa, int splits, half* out,
-                                             int d) {
+                                             float* sm, float* sl) {
+  for (int s = threadIdx.x; s < splits; s += blockDim.x) {
+    sm[s] = __ldcg(pm + s);
+    sl[s] = __ldcg(pl + s);
+  }
+  __syncthreads();
+  const int d = threadIdx.x;
+  if (d >= kHeadDim) return;
   float m = -INFINITY;
-  for (int s = 0; s < splits; ++s) m = fmaxf(m, __ldcg(pm + s));
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, sm[s]);
   float num = 0.f, den = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float l = __ldcg(pl + s);
-    if (l > 0.f) {
-      const float w = __expf(__ldcg(pm + s) - m);
-      num = fmaf(__ldcg(pa + s * kHeadDim + d), w, num);
-      den = fmaf(l, w, den);
+  for (int s0 = 0; s0 < splits; s0 += 16) {
+    float a[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a[j] = (s0 + j < splits) ? __ldcg(pa + (s0 + j) * kHeadDim + d) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int s = s0 + j;
+      if (s < splits && sl[s] > 0.f) {
+        const float w = __expf(sm[s] - m);
+        num = fmaf(a[j], w, num);
+        den = fmaf(sl[s], w, den);
+      }
     }
   }
   out[d] = __float2half(num / den);
@@ -176,6 +195,8 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   __shared__ float red[4];
   __shared__ __align__(8) uint64_t bar;
   __shared__ int last_cta;
+  __shared__ float comb_m[kMaxSplits];
+  __shared__ float comb_l[kMaxSplits];
 
   const int head = blockIdx.x;
   const int split = blockIdx.y;
@@ -274,12 +295,10 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   __syncthreads();
   if (!last_cta) return;
   __threadfence();
-  if (threadIdx.x < kHeadDim) {
-    combine_head(p.part_m + head * splits, p.part_l + head * splits,
-                 p.part_acc + static_cast<size_t>(head) * splits * kHeadDim, splits, p.out + head * kHeadDim,
-                 threadIdx.x);
-  }
   if (threadIdx.x == 0) p.counters[head] = 0u;
+  combine_head(p.part_m + head * splits, p.part_l + head * splits,
+               p.part_acc + static_cast<size_t>(head) * splits * kHeadDim, splits, p.out + head * kHeadDim, comb_m,
+               comb_l);
 }
 
 // Separate combine, used by the reference-compatible entry point.
@@ -287,11 +306,13 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
                                                           const float* __restrict__ part_l,
                                                           const float* __restrict__ part_acc, half* __restrict__ out,
                                                           int splits) {
+  __shared__ float comb_m[kMaxSplits];
+  __shared__ float comb_l[kMaxSplits];
   pdl_wait();
   pdl_trigger();
   const int head = blockIdx.x;
   combine_head(part_m + head * splits, part_l + head * splits, part_acc + static_cast<size_t>(head) * splits * kHeadDim,
-               splits, out + head * kHeadDim, threadIdx.x);
+               splits, out + head * kHeadDim, comb_m, comb_l);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -804,6 +825,8 @@ int fw_decode_attention(const void* q, void* k, void* v, void* out, const int64_
   FW_REQUIRE((k_new != nullptr) == (v_new != nullptr) && (k_new != nullptr) == (len_state != nullptr), FW_ERR_ARG,
              "len_state, k_new and v_new must be given together");
   FW_REQUIRE(heads > 0 && max_len > 0, FW_ERR_SHAPE, "k, v must be [heads, max_len, 64]");
+  FW_REQUIRE(max_len <= kMaxSplits * kSplitKeys, FW_ERR_SHAPE, "decode_attention: max_len must be <= %d",
+             kMaxSplits * kSplitKeys);
   const int splits = (max_len + kSplitKeys - 1) / kSplitKeys;
   FW_REQUIRE(part_m_numel >= int64_t(heads) * splits && part_l_numel >= int64_t(heads) * splits &&
                  part_acc_numel >= int64_t(heads) * splits * kHeadDim,
@@ -828,6 +851,8 @@ int fw_decode_attention_noalloc(const void* q, void* k, void* v, void* out, cons
   FW_REQUIRE((k_new != nullptr) == (v_new != nullptr) && (k_new != nullptr) == (len_state != nullptr), FW_ERR_ARG,
              "len_state, k_new and v_new must be given together");
   FW_REQUIRE(heads > 0 && max_len > 0, FW_ERR_SHAPE, "k, v must be [heads, max_len, 64]");
+  FW_REQUIRE(max_len <= kMaxSplits * kSplitKeys, FW_ERR_SHAPE, "decode_attention: max_len must be <= %d",
+             kMaxSplits * kSplitKeys);
   const int splits = (max_len + kSplitKeys - 1) / kSplitKeys;
   FW_REQUIRE(int64_t(heads) * splits <= kNoAllocMaxSlots, FW_ERR_SHAPE,
              "decode_attention_noalloc: heads * ceil(max_len / 64) = %lld exceeds the fixed scratch of %d "
@@ -966,6 +991,8 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
   FW_REQUIRE(d->prompt_len == 0 || d->prompt != nullptr, FW_ERR_NULL, "decoder_step: prompt is NULL");
   const int self_splits = (d->max_pos + kSplitKeys - 1) / kSplitKeys;
   const int cross_splits = (d->enc_len + kSplitKeys - 1) / kSplitKeys;
+  FW_REQUIRE(self_splits <= kMaxSplits && cross_splits <= kMaxSplits, FW_ERR_SHAPE,
+             "decoder_step: max_pos and enc_len must be <= %d", kMaxSplits * kSplitKeys);
   FW_REQUIRE(d->ws_splits >= self_splits && d->ws_splits >= cross_splits, FW_ERR_SHAPE,
              "decoder_step: workspace too small for %d splits", cross_splits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
