@@ -28,22 +28,35 @@ FW_DEFINE_ERROR_WORD();
 __device__ __forceinline__ void flag_error(unsigned bits) { atomicOr(&g_fw_dev_error, bits); }
 
 // ---------------------------------------------------------------------------------------------
+// Block-level synchronisation of the 256 compute threads. Stand-alone kernels use __syncthreads;
+// the persistent decode kernel (which also runs a producer warp that never joins) uses named
+// barrier 1 over exactly the 256 compute threads.
+template <bool kNamed>
+__device__ __forceinline__ void compute_sync() {
+  if (kNamed)
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+  else
+    __syncthreads();
+}
+
 // LayerNorm over 1280 values held 5 per thread by a 256-thread block (index tid + 256*i).
 // Summation order matches add_layernorm_kernel (custom/kernels/whisper_kernels.cu:217-267):
 // per-thread running sums, warp xor-tree, then the eight warp partials in order.
+template <bool kNamed = false>
 __device__ __forceinline__ void ln1280_stats(const float (&v)[5], float* red, float eps, float& mean, float& inv) {
+  // red: 16 floats, [0, 8) warp sums, [8, 16) warp sums of squares. The caller separates two calls
+  // with a barrier of its own.
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < 5; ++i) sum += v[i];
   sum = warp_sum(sum);
   if (lane == 0) red[warp] = sum;
-  __syncthreads();
+  compute_sync<kNamed>();
   float m = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) m += red[i];
   m /= static_cast<float>(kHidden);
-  __syncthreads();
   float sq = 0.f;
 #pragma unroll
   for (int i = 0; i < 5; ++i) {
@@ -51,14 +64,13 @@ __device__ __forceinline__ void ln1280_stats(const float (&v)[5], float* red, fl
     sq = fmaf(d, d, sq);
   }
   sq = warp_sum(sq);
-  if (lane == 0) red[warp] = sq;
-  __syncthreads();
+  if (lane == 0) red[8 + warp] = sq;
+  compute_sync<kNamed>();
   float var = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) var += red[i];
+  for (int i = 0; i < 8; ++i) var += red[8 + i];
   mean = m;
   inv = rsqrtf(var / static_cast<float>(kHidden) + eps);
-  __syncthreads();
 }
 
 __device__ __forceinline__ float ln_apply(float v, float mean, float inv, float g, float b) {
@@ -106,7 +118,7 @@ __global__ void __launch_bounds__(256) add_layernorm_kernel(half* __restrict__ h
                                                             const half* __restrict__ gamma,
                                                             const half* __restrict__ beta, half* __restrict__ y,
                                                             float eps) {
-  __shared__ float red[8];
+  __shared__ float red[16];
   pdl_wait();
   pdl_trigger();
   float v[5];
@@ -187,30 +199,165 @@ __device__ __forceinline__ void combine_head(const float* pm, const float* pl, c
   out[d] = __float2half(num / den);
 }
 
-__global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
+// Scratch of one 64-key attention split processed by 64 threads. 16-byte aligned (and so padded)
+// because `q` is read as float4 and the persistent kernel keeps an array of four.
+struct __align__(16) UnitScratch {
+  float q[kHeadDim];
+  float sc[kSplitKeys];
+  float pacc[4][kHeadDim];
+  float red[4];
+  float comb_m[kMaxSplits];
+  float comb_l[kMaxSplits];
+  int last;
+};
+
+// Barrier of the 64 threads that process one split: the whole CTA of the stand-alone kernel (id 0)
+// or named barrier `id` (a pair of warps) inside the persistent kernel.
+__device__ __forceinline__ void unit_sync(int id) {
+  if (id == 0)
+    __syncthreads();
+  else
+    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+
+// One 64-key split of one head (whisper_kernels.cu:108-189) on 64 threads, t = 0..63. Thread t
+// scores key t over all 64 dims; the 32 pair products fmaf(q0*k0 + q1*k1) are summed in exactly the
+// pairing of the reference's warp xor-tree (offsets 16, 8, 4, 2, 1), and the value accumulation keeps
+// the reference's per-warp residue classes (keys i = r mod 4, r = 0..3) and their final order, so the
+// partial (m, l, acc) is bit-identical to the reference kernel's while the score pass no longer
+// serialises a shuffle reduction per key. K rows are read with a per-thread chunk rotation so the
+// 16-byte shared loads are bank-conflict free.
+__device__ __forceinline__ void attn_unit64(const half* q, const half* ks, const half* vs, int n, float scale, int t,
+                                            UnitScratch& U, int sync_id, float* part_acc, float* part_m,
+                                            float* part_l) {
+  const int lane = t & 31, wa = t >> 5;
+  if (t < 32) {
+    const float2 qf = __half22float2(__ldcg(reinterpret_cast<const half2*>(q) + t));
+    U.q[2 * t] = qf.x;
+    U.q[2 * t + 1] = qf.y;
+  }
+  unit_sync(sync_id);
+  float s = -INFINITY;
+  if (t < n) {
+    const uint4* kr = reinterpret_cast<const uint4*>(ks + t * kHeadDim);
+    float pj[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = (j + t) & 7;
+      const uint4 kv = kr[c];
+      const half2* h2 = reinterpret_cast<const half2*>(&kv);
+      const float4 qa = *reinterpret_cast<const float4*>(&U.q[8 * c]);
+      const float4 qb = *reinterpret_cast<const float4*>(&U.q[8 * c + 4]);
+      const float2 k0 = __half22float2(h2[0]), k1 = __half22float2(h2[1]);
+      const float2 k2 = __half22float2(h2[2]), k3 = __half22float2(h2[3]);
+      pj[j][0] = fmaf(qa.x, k0.x, qa.y * k0.y);
+      pj[j][1] = fmaf(qa.z, k1.x, qa.w * k1.y);
+      pj[j][2] = fmaf(qb.x, k2.x, qb.y * k2.y);
+      pj[j][3] = fmaf(qb.z, k3.x, qb.w * k3.y);
+    }
+    // xor-tree pairing: chunk c with c^4, then c^2, then c^1 (rotation keeps the pairs), then
+    // within the chunk e with e^2 and e^1
+    float a[4][4], b[2][4], cc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) a[j][e] = pj[j][e] + pj[j + 4][e];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) b[j][e] = a[j][e] + a[j + 2][e];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) cc[e] = b[0][e] + b[1][e];
+    s = ((cc[0] + cc[2]) + (cc[1] + cc[3])) * scale;
+  }
+  const float wmax = warp_max(s);
+  if (lane == 0) U.red[wa] = wmax;
+  unit_sync(sync_id);
+  const float m = fmaxf(U.red[0], U.red[1]);
+  float e = 0.f;
+  if (t < n) {
+    e = __expf(s - m);
+    U.sc[t] = e;
+  }
+  e = warp_sum(e);
+  if (lane == 0) U.red[2 + wa] = e;
+  unit_sync(sync_id);
+  // value accumulation: warp wa owns residues wa and wa + 2
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+  for (int i = wa; i < n; i += 4) {
+    const float2 v0 = __half22float2(reinterpret_cast<const half2*>(vs + i * kHeadDim)[lane]);
+    const float p0 = U.sc[i];
+    acc0.x = fmaf(p0, v0.x, acc0.x);
+    acc0.y = fmaf(p0, v0.y, acc0.y);
+    if (i + 2 < n) {
+      const float2 v1 = __half22float2(reinterpret_cast<const half2*>(vs + (i + 2) * kHeadDim)[lane]);
+      const float p1 = U.sc[i + 2];
+      acc1.x = fmaf(p1, v1.x, acc1.x);
+      acc1.y = fmaf(p1, v1.y, acc1.y);
+    }
+  }
+  U.pacc[wa][2 * lane] = acc0.x;
+  U.pacc[wa][2 * lane + 1] = acc0.y;
+  U.pacc[wa + 2][2 * lane] = acc1.x;
+  U.pacc[wa + 2][2 * lane + 1] = acc1.y;
+  unit_sync(sync_id);
+  part_acc[t] = ((U.pacc[0][t] + U.pacc[1][t]) + U.pacc[2][t]) + U.pacc[3][t];
+  if (t == 0) {
+    *part_m = m;
+    *part_l = U.red[2] + U.red[3];
+  }
+}
+
+// Combine of one head by the 64 threads of a unit (same arithmetic as combine_head).
+__device__ __forceinline__ void combine_unit64(UnitScratch& U, int sync_id, int t, const float* pm, const float* pl,
+                                               const float* pa, int splits, half* out) {
+  for (int s = t; s < splits; s += 64) {
+    U.comb_m[s] = __ldcg(pm + s);
+    U.comb_l[s] = __ldcg(pl + s);
+  }
+  unit_sync(sync_id);
+  float m = -INFINITY;
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, U.comb_m[s]);
+  float num = 0.f, den = 0.f;
+  for (int s0 = 0; s0 < splits; s0 += 16) {
+    float a[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a[j] = (s0 + j < splits) ? __ldcg(pa + (s0 + j) * kHeadDim + t) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int s = s0 + j;
+      if (s < splits && U.comb_l[s] > 0.f) {
+        const float w = __expf(U.comb_m[s] - m);
+        num = fmaf(a[j], w, num);
+        den = fmaf(U.comb_l[s], w, den);
+      }
+    }
+  }
+  out[t] = __float2half(num / den);
+}
+
+// Split-K single-query attention, one 64-key split per 64-thread CTA. The split's K and V rows are
+// bulk-copied into shared memory before griddepcontrol.wait (cache rows below the current position
+// and the cross-attention cache are never written by the previous kernel). With `counters` set, the
+// last CTA of each head to finish merges the splits (atomic arrival counter, nothing spins).
+__global__ void __launch_bounds__(64) attn_split_kernel(AttnParams p) {
   __shared__ __align__(128) half ks[kSplitKeys * kHeadDim];
   __shared__ __align__(128) half vs[kSplitKeys * kHeadDim];
-  __shared__ float scores[kSplitKeys];
-  __shared__ float partial[4][kHeadDim];
-  __shared__ float red[4];
+  __shared__ __align__(16) UnitScratch U;
   __shared__ __align__(8) uint64_t bar;
-  __shared__ int last_cta;
-  __shared__ float comb_m[kMaxSplits];
-  __shared__ float comb_l[kMaxSplits];
 
   const int head = blockIdx.x;
   const int split = blockIdx.y;
   const int splits = gridDim.y;
   const int slot = head * splits + split;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
 
   int pos = -1;
   int len = p.max_len;
   if (p.len_state) {
     const int64_t raw = p.len_state[0];
     pos = static_cast<int>(raw < 0 ? 0 : (raw >= p.max_len ? p.max_len - 1 : raw));
-    if (threadIdx.x == 0 && split == 0 && head == 0 && (raw < 0 || raw >= p.max_len)) flag_error(FW_DEVERR_BAD_INDEX);
+    if (t == 0 && split == 0 && head == 0 && (raw < 0 || raw >= p.max_len)) flag_error(FW_DEVERR_BAD_INDEX);
     len = pos + 1;
   }
   const int begin = split * kSplitKeys;
@@ -218,7 +365,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   half* kh = p.k + static_cast<size_t>(head) * p.max_len * kHeadDim;
   half* vh = p.v + static_cast<size_t>(head) * p.max_len * kHeadDim;
 
-  if (threadIdx.x == 0) {
+  if (t == 0) {
     mbar_init(&bar, 1);
     mbar_fence_init();
     if (n > 0) {
@@ -234,56 +381,18 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
 
   if (n > 0) {
     if (!mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
-    const half2* kn = p.k_new ? reinterpret_cast<const half2*>(p.k_new + head * kHeadDim) : nullptr;
-    const half2* vn = p.v_new ? reinterpret_cast<const half2*>(p.v_new + head * kHeadDim) : nullptr;
-    if (kn && warp == 0 && pos >= begin && pos < begin + n) {
-      const half2 kv = kn[lane], vv = vn[lane];
+    if (p.k_new && warp == 0 && pos >= begin && pos < begin + n) {
+      const half2 kv = reinterpret_cast<const half2*>(p.k_new + head * kHeadDim)[lane];
+      const half2 vv = reinterpret_cast<const half2*>(p.v_new + head * kHeadDim)[lane];
       reinterpret_cast<half2*>(kh + static_cast<size_t>(pos) * kHeadDim)[lane] = kv;  // fused cache write
       reinterpret_cast<half2*>(vh + static_cast<size_t>(pos) * kHeadDim)[lane] = vv;
       reinterpret_cast<half2*>(ks + (pos - begin) * kHeadDim)[lane] = kv;
       reinterpret_cast<half2*>(vs + (pos - begin) * kHeadDim)[lane] = vv;
     }
     __syncthreads();
-    const float2 qf = __half22float2(reinterpret_cast<const half2*>(p.q + head * kHeadDim)[lane]);
-    for (int i = warp; i < n; i += 4) {
-      const float2 kf = __half22float2(reinterpret_cast<const half2*>(ks + i * kHeadDim)[lane]);
-      const float s = warp_sum(fmaf(qf.x, kf.x, qf.y * kf.y)) * p.scale;
-      if (lane == 0) scores[i] = s;
-    }
-    __syncthreads();
-    const float s = threadIdx.x < n ? scores[threadIdx.x] : -INFINITY;
-    float wmax = warp_max(s);
-    if (lane == 0) red[warp] = wmax;
-    __syncthreads();
-    const float m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    __syncthreads();
-    float e = 0.f;
-    if (threadIdx.x < n) {
-      e = __expf(s - m);
-      scores[threadIdx.x] = e;
-    }
-    e = warp_sum(e);
-    if (lane == 0) red[warp] = e;
-    __syncthreads();
-    float2 acc = make_float2(0.f, 0.f);
-    for (int i = warp; i < n; i += 4) {
-      const float2 vf = __half22float2(reinterpret_cast<const half2*>(vs + i * kHeadDim)[lane]);
-      const float pr = scores[i];
-      acc.x = fmaf(pr, vf.x, acc.x);
-      acc.y = fmaf(pr, vf.y, acc.y);
-    }
-    partial[warp][2 * lane] = acc.x;
-    partial[warp][2 * lane + 1] = acc.y;
-    __syncthreads();
-    if (threadIdx.x < kHeadDim) {
-      p.part_acc[static_cast<size_t>(slot) * kHeadDim + threadIdx.x] =
-          partial[0][threadIdx.x] + partial[1][threadIdx.x] + partial[2][threadIdx.x] + partial[3][threadIdx.x];
-    }
-    if (threadIdx.x == 0) {
-      p.part_m[slot] = m;
-      p.part_l[slot] = red[0] + red[1] + red[2] + red[3];
-    }
-  } else if (threadIdx.x == 0) {
+    attn_unit64(p.q + head * kHeadDim, ks, vs, n, p.scale, t, U, 0, p.part_acc + static_cast<size_t>(slot) * kHeadDim,
+                p.part_m + slot, p.part_l + slot);
+  } else if (t == 0) {
     p.part_m[slot] = -INFINITY;
     p.part_l[slot] = 0.f;
   }
@@ -291,14 +400,13 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   if (p.counters == nullptr) return;
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last_cta = atomicAdd(p.counters + head, 1u) == static_cast<unsigned>(splits - 1);
+  if (t == 0) U.last = atomicAdd(p.counters + head, 1u) == static_cast<unsigned>(splits - 1);
   __syncthreads();
-  if (!last_cta) return;
+  if (!U.last) return;
   __threadfence();
-  if (threadIdx.x == 0) p.counters[head] = 0u;
-  combine_head(p.part_m + head * splits, p.part_l + head * splits,
-               p.part_acc + static_cast<size_t>(head) * splits * kHeadDim, splits, p.out + head * kHeadDim, comb_m,
-               comb_l);
+  if (t == 0) p.counters[head] = 0u;
+  combine_unit64(U, 0, t, p.part_m + head * splits, p.part_l + head * splits,
+                 p.part_acc + static_cast<size_t>(head) * splits * kHeadDim, splits, p.out + head * kHeadDim);
 }
 
 // Separate combine, used by the reference-compatible entry point.
@@ -369,7 +477,7 @@ template <bool kLN, bool kFinalize>
 __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kLmStages];
-  __shared__ float red[8];
+  __shared__ float red[16];
   __shared__ __align__(16) half ys[kHidden];
   __shared__ unsigned long long warp_best[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -504,7 +612,7 @@ template <bool kEmbed, int kAct>
 __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
-  __shared__ float red[8];
+  __shared__ float red[16];
   __shared__ __align__(16) half ys[kHidden];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r0 = blockIdx.x * p.rows_per_cta;
@@ -737,7 +845,7 @@ static int launch_gemv_residual(const GemvParams& p, cudaStream_t s, bool pdl) {
 }
 
 static int launch_attention(const AttnParams& p, int heads, int splits, cudaStream_t s, bool pdl) {
-  cudaError_t e = launch(attn_split_kernel, dim3(heads, splits), dim3(128), 0, s, pdl, p);
+  cudaError_t e = launch(attn_split_kernel, dim3(heads, splits), dim3(64), 0, s, pdl, p);
   return launch_status(e, "decode_attention");
 }
 
@@ -996,6 +1104,7 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
   FW_REQUIRE(d->ws_splits >= self_splits && d->ws_splits >= cross_splits, FW_ERR_SHAPE,
              "decoder_step: workspace too small for %d splits", cross_splits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (steps <= 0) return FW_OK;
   half* h = static_cast<half*>(d->h);
   half* qkv = static_cast<half*>(d->qkv);
   half* attn = static_cast<half*>(d->attn);
