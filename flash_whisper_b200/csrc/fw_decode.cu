@@ -16,12 +16,16 @@
 // kernel N overlaps the tail of kernel N-1. Dot products use the same per-lane order and warp
 // xor-tree as the reference kernels so that the LM-head logits, LayerNorm outputs and attention
 // outputs are bit-identical to the reference kernels given identical inputs.
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "fw_common.cuh"
 #include "fw_host.h"
 
 namespace fw {
+
+namespace cg = cooperative_groups;
 
 FW_DEFINE_ERROR_WORD();
 
@@ -200,19 +204,24 @@ __device__ __forceinline__ void combine_head(const float* pm, const float* pl, c
 }
 
 // Scratch of one 64-key attention split processed by 64 threads. 16-byte aligned (and so padded)
-// because `q` is read as float4 and the persistent kernel keeps an array of four.
-struct __align__(16) UnitScratch {
+// because `q` is read as float4.
+struct __align__(16) SplitScratch {
   float q[kHeadDim];
   float sc[kSplitKeys];
   float pacc[4][kHeadDim];
   float red[4];
+};
+
+// Split scratch plus the staging arrays of the last-CTA combine of attn_split_kernel.
+struct __align__(16) UnitScratch {
+  SplitScratch s;
   float comb_m[kMaxSplits];
   float comb_l[kMaxSplits];
   int last;
 };
 
 // Barrier of the 64 threads that process one split: the whole CTA of the stand-alone kernel (id 0)
-// or named barrier `id` (a pair of warps) inside the persistent kernel.
+// or named barrier `id` (a pair of warps) inside a larger CTA.
 __device__ __forceinline__ void unit_sync(int id) {
   if (id == 0)
     __syncthreads();
@@ -220,23 +229,18 @@ __device__ __forceinline__ void unit_sync(int id) {
     asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
 }
 
-// One 64-key split of one head (whisper_kernels.cu:108-189) on 64 threads, t = 0..63. Thread t
-// scores key t over all 64 dims; the 32 pair products fmaf(q0*k0 + q1*k1) are summed in exactly the
-// pairing of the reference's warp xor-tree (offsets 16, 8, 4, 2, 1), and the value accumulation keeps
-// the reference's per-warp residue classes (keys i = r mod 4, r = 0..3) and their final order, so the
+// One 64-key split of one head (whisper_kernels.cu:108-189) on 64 threads, t = 0..63, with the
+// query already in U.q (fp32, made visible to the 64 threads by the caller). Thread t scores key t
+// over all 64 dims; the 32 pair products fmaf(q0*k0 + q1*k1) are summed in exactly the pairing of
+// the reference's warp xor-tree (offsets 16, 8, 4, 2, 1), and the value accumulation keeps the
+// reference's per-warp residue classes (keys i = r mod 4, r = 0..3) and their final order, so the
 // partial (m, l, acc) is bit-identical to the reference kernel's while the score pass no longer
 // serialises a shuffle reduction per key. K rows are read with a per-thread chunk rotation so the
-// 16-byte shared loads are bank-conflict free.
-__device__ __forceinline__ void attn_unit64(const half* q, const half* ks, const half* vs, int n, float scale, int t,
-                                            UnitScratch& U, int sync_id, float* part_acc, float* part_m,
-                                            float* part_l) {
+// 16-byte shared loads are bank-conflict free. part_* may point into another CTA's shared memory.
+template <int kCopies = 1>
+__device__ __forceinline__ void attn_unit64(const half* ks, const half* vs, int n, float scale, int t, SplitScratch& U,
+                                            int sync_id, float* part_acc, float* part_m, float* part_l) {
   const int lane = t & 31, wa = t >> 5;
-  if (t < 32) {
-    const float2 qf = __half22float2(__ldcg(reinterpret_cast<const half2*>(q) + t));
-    U.q[2 * t] = qf.x;
-    U.q[2 * t + 1] = qf.y;
-  }
-  unit_sync(sync_id);
   float s = -INFINITY;
   if (t < n) {
     const uint4* kr = reinterpret_cast<const uint4*>(ks + t * kHeadDim);
@@ -301,10 +305,24 @@ __device__ __forceinline__ void attn_unit64(const half* q, const half* ks, const
   U.pacc[wa + 2][2 * lane] = acc1.x;
   U.pacc[wa + 2][2 * lane + 1] = acc1.y;
   unit_sync(sync_id);
-  part_acc[t] = ((U.pacc[0][t] + U.pacc[1][t]) + U.pacc[2][t]) + U.pacc[3][t];
-  if (t == 0) {
-    *part_m = m;
-    *part_l = U.red[2] + U.red[3];
+  const float a = ((U.pacc[0][t] + U.pacc[1][t]) + U.pacc[2][t]) + U.pacc[3][t];
+  const float l = U.red[2] + U.red[3];
+  if (kCopies == 1) {
+    part_acc[t] = a;
+    if (t == 0) {
+      *part_m = m;
+      *part_l = l;
+    }
+  } else {  // part_* are this CTA's shared arrays; the same slot is written in every CTA of the cluster
+    cg::cluster_group cluster = cg::this_cluster();
+#pragma unroll
+    for (int r = 0; r < kCopies; ++r) {
+      cluster.map_shared_rank(part_acc, r)[t] = a;
+      if (t == 0) {
+        *cluster.map_shared_rank(part_m, r) = m;
+        *cluster.map_shared_rank(part_l, r) = l;
+      }
+    }
   }
 }
 
@@ -389,9 +407,14 @@ __global__ void __launch_bounds__(64) attn_split_kernel(AttnParams p) {
       reinterpret_cast<half2*>(ks + (pos - begin) * kHeadDim)[lane] = kv;
       reinterpret_cast<half2*>(vs + (pos - begin) * kHeadDim)[lane] = vv;
     }
+    if (t < 32) {
+      const float2 qf = __half22float2(__ldcg(reinterpret_cast<const half2*>(p.q + head * kHeadDim) + t));
+      U.s.q[2 * t] = qf.x;
+      U.s.q[2 * t + 1] = qf.y;
+    }
     __syncthreads();
-    attn_unit64(p.q + head * kHeadDim, ks, vs, n, p.scale, t, U, 0, p.part_acc + static_cast<size_t>(slot) * kHeadDim,
-                p.part_m + slot, p.part_l + slot);
+    attn_unit64(ks, vs, n, p.scale, t, U.s, 0, p.part_acc + static_cast<size_t>(slot) * kHeadDim, p.part_m + slot,
+                p.part_l + slot);
   } else if (t == 0) {
     p.part_m[slot] = -INFINITY;
     p.part_l[slot] = 0.f;
@@ -421,6 +444,309 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
   const int head = blockIdx.x;
   combine_head(part_m + head * splits, part_l + head * splits, part_acc + static_cast<size_t>(head) * splits * kHeadDim,
                splits, out + head * kHeadDim, comb_m, comb_l);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Attention block of one decoder layer, one thread-block cluster per head. The reference runs
+// add_layernorm -> F.linear (q/k/v) -> decode_attention (split + combine) -> F.linear (out_proj)
+// -> residual add as five or six launches (custom/model.py:113-116 self, :116-119 cross). Here the
+// whole chain is one launch: cluster `head` (kHeadCtas CTAs) computes
+//   1. LN(h) and this head's projection rows (q, k, v for self attention; q for cross), split over
+//      the cluster's CTAs and broadcast into every CTA's shared memory (DSMEM);
+//   2. the 64-key attention splits of this head (self: one per CTA, with the fused cache write;
+//      cross: up to kHeadMaxUnits per CTA on 64-thread units), each split's (m, l, acc) broadcast
+//      to every CTA;
+//   3. the split combine in every CTA (same arithmetic and order as the reference combine);
+//   4. this head's slice of the output projection, W_o[:, head] . o_head, for 1280 / kHeadCtas rows
+//      per CTA, written as fp32 partials [heads, 1280];
+//   5. the residual update: the last of the `heads` CTAs that hold the same row block (atomic
+//      arrival counter per block, nothing spins) sums the per-head partials in head order, adds the
+//      bias and the residual: h[r] = fp16(h[r] + fp16(sum + b[r])).
+// Weight rows, the K/V splits and the output-projection slice (head-major [heads, 1280, 64]) are
+// bulk-copied into shared memory before griddepcontrol.wait. Only two cluster barriers are needed,
+// after which no CTA touches another CTA's shared memory.
+constexpr int kHeadCtas = 8;                              // CTAs per head cluster
+constexpr int kHeadMaxUnits = 3;                          // attention splits per CTA (cross: 24 / 8)
+constexpr int kOutRows = kHidden / kHeadCtas;             // output-projection rows per CTA (160)
+constexpr int kSelfProjRows = 3 * kHeadDim / kHeadCtas;   // q, k, v rows per CTA (24)
+constexpr int kCrossProjRows = kHeadDim / kHeadCtas;      // q rows per CTA (8)
+
+struct HeadBlockParams {
+  half* h;  // residual stream [1280]: LN input, updated in place by the last CTAs
+  const half* gamma;
+  const half* beta;
+  float eps;
+  // layer-0 prologue: h is built from the token embedding and learned position instead of read
+  const half* embed;
+  const half* pos_embed;
+  const int64_t* cur;
+  const int64_t* prompt;
+  int prompt_len;
+  int vocab;
+  const int64_t* state;  // [position, count]; self attention length = position + 1
+  int max_pos;
+  bool state_early;  // position may be read before griddepcontrol.wait (no in-flight kernel writes it)
+  // projection (self: [3840, 1280] q|k|v rows; cross: [1280, 1280] q rows) and its bias
+  const half* w;
+  const half* b;
+  // attention cache [heads, kv_len, 64]
+  half* k;
+  half* v;
+  int kv_len;
+  float scale;
+  // output projection, head-major [heads, 1280, 64], and its bias [1280]
+  const half* wo;
+  const half* bo;
+  float* part;            // fp32 [heads, 1280] per-head output-projection partials
+  unsigned int* counter;  // [kHeadCtas] arrival counters, zero before, left zero
+  half* attn_out;         // optional [heads * 64] attention output (written by rank 0)
+};
+
+template <bool kSelf>
+struct HeadBlockShape {
+  static constexpr int kProjRows = kSelf ? kSelfProjRows : kCrossProjRows;
+  static constexpr int kUnits = kSelf ? 1 : kHeadMaxUnits;
+  static constexpr int kSlots = kHeadCtas * kUnits;
+  static constexpr int kProjBytes = kProjRows * kHidden * 2;
+  static constexpr int kKvBytes = kUnits * 2 * kSplitKeys * kHeadDim * 2;
+  static constexpr int kOutBytes = kOutRows * kHeadDim * 2;
+  static constexpr int kSmem = kProjBytes + kKvBytes + kOutBytes;
+};
+
+template <bool kSelf, bool kEmbed>
+__global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
+  using S = HeadBlockShape<kSelf>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar_w, bar_kv, bar_o;
+  __shared__ float red[16];
+  __shared__ __align__(16) half ys[kHidden];
+  __shared__ __align__(16) half hs[kHidden];                   // residual-stream input (for step 5)
+  __shared__ __align__(16) half qv[S::kProjRows * kHeadCtas];  // this head's q (| k | v)
+  __shared__ __align__(16) float os[kHeadDim];                  // this head's attention output
+  __shared__ __align__(16) SplitScratch U[S::kUnits];
+  __shared__ float sm_m[S::kSlots];
+  __shared__ float sm_l[S::kSlots];
+  __shared__ __align__(16) float sm_acc[S::kSlots][kHeadDim];
+  __shared__ int s_last;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = blockIdx.x;  // cluster dims (kHeadCtas, 1, 1) over grid (kHeadCtas, heads)
+  const int head = blockIdx.y;
+  const int heads = gridDim.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  half* wproj = reinterpret_cast<half*>(smem);
+  half* kvs = reinterpret_cast<half*>(smem + S::kProjBytes);
+  half* wout = reinterpret_cast<half*>(smem + S::kProjBytes + S::kKvBytes);
+  const int splits = (p.kv_len + kSplitKeys - 1) / kSplitKeys;
+  half* kh = p.k + static_cast<size_t>(head) * p.kv_len * kHeadDim;
+  half* vh = p.v + static_cast<size_t>(head) * p.kv_len * kHeadDim;
+
+  // global projection row of local row j (0 <= j < kProjRows * kHeadCtas)
+  auto proj_row = [&](int j) {
+    return kSelf ? (j / kHeadDim) * kHidden + head * kHeadDim + (j % kHeadDim) : head * kHeadDim + j;
+  };
+
+  // Attention length: self = position + 1 (position read early only when no in-flight kernel
+  // writes it), cross = kv_len.
+  int pos = 0, len = p.kv_len;
+  bool pos_known = !kSelf;
+  if (kSelf && p.state_early) {
+    pos = static_cast<int>(min(max(p.state[0], int64_t(0)), int64_t(p.max_pos - 1)));
+    len = pos + 1;
+    pos_known = true;
+  }
+
+  if (tid == 0) {
+    mbar_init(&bar_w, 1);
+    mbar_init(&bar_kv, 1);
+    mbar_init(&bar_o, 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(&bar_w, S::kProjBytes);
+    for (int r = 0; r < S::kProjRows; ++r)
+      bulk_g2s(wproj + r * kHidden, p.w + static_cast<size_t>(proj_row(rank * S::kProjRows + r)) * kHidden,
+               kHidden * 2, &bar_w);
+    // K/V rows of this CTA's splits: the keys below the attention length (all of them while the
+    // length is not yet known; rows past it are fetched but not used). A unit that attends over
+    // n > 0 keys after the wait always had its rows requested here, so it may wait on bar_kv.
+    int nkv[S::kUnits];
+    unsigned kv_bytes = 0;
+    for (int u = 0; u < S::kUnits; ++u) {
+      const int begin = (rank * S::kUnits + u) * kSplitKeys;
+      nkv[u] = max(0, min(kSplitKeys, (pos_known ? len : p.kv_len) - begin));
+      kv_bytes += 2u * static_cast<unsigned>(nkv[u]) * kHeadDim * 2;
+    }
+    if (kv_bytes) {
+      mbar_arrive_expect_tx(&bar_kv, kv_bytes);
+      for (int u = 0; u < S::kUnits; ++u) {
+        if (nkv[u] == 0) continue;
+        const int begin = (rank * S::kUnits + u) * kSplitKeys;
+        const unsigned bytes = static_cast<unsigned>(nkv[u]) * kHeadDim * 2;
+        bulk_g2s(kvs + (2 * u) * kSplitKeys * kHeadDim, kh + static_cast<size_t>(begin) * kHeadDim, bytes, &bar_kv);
+        bulk_g2s(kvs + (2 * u + 1) * kSplitKeys * kHeadDim, vh + static_cast<size_t>(begin) * kHeadDim, bytes,
+                 &bar_kv);
+      }
+    }
+    mbar_arrive_expect_tx(&bar_o, S::kOutBytes);
+    bulk_g2s(wout, p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes, &bar_o);
+  }
+  // LayerNorm parameters and biases are weights: loaded before the wait, into registers
+  constexpr int kRowsPerWarp = (S::kProjRows + 7) / 8;
+  float g[5], be[5], pbias[kRowsPerWarp];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    g[i] = __half2float(p.gamma[tid + i * 256]);
+    be[i] = __half2float(p.beta[tid + i * 256]);
+  }
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int r = warp + 8 * i;
+    pbias[i] = (p.b && r < S::kProjRows) ? __half2float(p.b[proj_row(rank * S::kProjRows + r)]) : 0.f;
+  }
+  const float obias = (p.bo && tid < kOutRows) ? __half2float(p.bo[rank * kOutRows + tid]) : 0.f;
+  __syncthreads();
+  cluster_arrive_relaxed();  // completed by the wait before the first DSMEM store: all CTAs are running
+  pdl_wait();
+  pdl_trigger();
+
+  // ---- 1. LayerNorm prologue and this CTA's projection rows ----
+  if (kEmbed || (kSelf && !p.state_early)) {
+    const int64_t raw = p.state[0];
+    if (raw < 0 || raw >= p.max_pos) {
+      if (tid == 0 && rank == 0 && head == 0) flag_error(FW_DEVERR_BAD_INDEX);
+    }
+    pos = static_cast<int>(min(max(raw, int64_t(0)), int64_t(p.max_pos - 1)));
+    len = pos + 1;
+  }
+  float v[5];
+  if (kEmbed) {
+    int64_t tok = (pos < p.prompt_len) ? p.prompt[pos] : p.cur[0];
+    if (tok < 0 || tok >= p.vocab) {
+      if (tid == 0 && rank == 0 && head == 0) flag_error(FW_DEVERR_BAD_INDEX);
+      tok = tok < 0 ? 0 : p.vocab - 1;
+    }
+    const half* er = p.embed + static_cast<size_t>(tok) * kHidden;
+    const half* pr = p.pos_embed + static_cast<size_t>(pos) * kHidden;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = round_half(__half2float(er[tid + i * 256]) + __half2float(pr[tid + i * 256]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = __half2float(p.h[tid + i * 256]);
+  }
+#pragma unroll
+  for (int i = 0; i < 5; ++i) hs[tid + i * 256] = __float2half(v[i]);  // exact: v holds fp16 values
+  float mean, inv;
+  ln1280_stats(v, red, p.eps, mean, inv);
+#pragma unroll
+  for (int i = 0; i < 5; ++i) ys[tid + i * 256] = __float2half(ln_apply(v[i], mean, inv, g[i], be[i]));
+  __syncthreads();
+  {
+    float xf[40];
+    load_x40(ys, xf);
+    if (!mbar_wait(&bar_w, 0)) flag_error(FW_DEVERR_TIMEOUT);
+    cluster_wait();
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const int r = warp + 8 * i;
+      if (r >= S::kProjRows) break;
+      const float acc = warp_sum(dot1280_lane(reinterpret_cast<const uint4*>(wproj + r * kHidden), xf));
+      if (lane < kHeadCtas)  // every lane holds the same sum; lane r stores into cluster rank r
+        *cluster.map_shared_rank(&qv[rank * S::kProjRows + r], lane) = __float2half(acc + pbias[i]);
+    }
+  }
+  cluster.sync();  // q (| k | v) of this head visible in every CTA
+
+  // ---- 2. attention splits ----
+  {
+    const int u = tid >> 6, t = tid & 63;
+    const int split = rank * S::kUnits + u;
+    if (u < S::kUnits && split < splits) {
+      const int begin = split * kSplitKeys;
+      const int n = min(kSplitKeys, len - begin);
+      half* ks = kvs + (2 * u) * kSplitKeys * kHeadDim;
+      half* vs = kvs + (2 * u + 1) * kSplitKeys * kHeadDim;
+      if (n > 0) {
+        if (!mbar_wait(&bar_kv, 0)) flag_error(FW_DEVERR_TIMEOUT);
+        if constexpr (kSelf) {
+          if (t < 32 && pos >= begin && pos < begin + n) {  // fused cache write of the new key/value
+            const half2 kn = reinterpret_cast<const half2*>(qv + kHeadDim)[t];
+            const half2 vn = reinterpret_cast<const half2*>(qv + 2 * kHeadDim)[t];
+            reinterpret_cast<half2*>(kh + static_cast<size_t>(pos) * kHeadDim)[t] = kn;
+            reinterpret_cast<half2*>(vh + static_cast<size_t>(pos) * kHeadDim)[t] = vn;
+            reinterpret_cast<half2*>(ks + (pos - begin) * kHeadDim)[t] = kn;
+            reinterpret_cast<half2*>(vs + (pos - begin) * kHeadDim)[t] = vn;
+          }
+        }
+        if (t < 32) {
+          const float2 qf = __half22float2(reinterpret_cast<const half2*>(qv)[t]);
+          U[u].q[2 * t] = qf.x;
+          U[u].q[2 * t + 1] = qf.y;
+        }
+        unit_sync(1 + u);
+        attn_unit64<kHeadCtas>(ks, vs, n, p.scale, t, U[u], 1 + u, &sm_acc[split][0], &sm_m[split], &sm_l[split]);
+      } else if (t == 0) {
+#pragma unroll
+        for (int r = 0; r < kHeadCtas; ++r) {
+          *cluster.map_shared_rank(&sm_m[split], r) = -INFINITY;
+          *cluster.map_shared_rank(&sm_l[split], r) = 0.f;
+        }
+      }
+    }
+  }
+  cluster.sync();  // every split's partial visible in every CTA; no DSMEM access after this point
+
+  // ---- 3. split combine (whisper_kernels.cu:193-213 order), in every CTA ----
+  if (tid < kHeadDim) {
+    float m = -INFINITY;
+    for (int s = 0; s < splits; ++s) m = fmaxf(m, sm_m[s]);
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      if (sm_l[s] > 0.f) {
+        const float w = __expf(sm_m[s] - m);
+        num = fmaf(sm_acc[s][tid], w, num);
+        den = fmaf(sm_l[s], w, den);
+      }
+    }
+    const half o = __float2half(num / den);
+    os[tid] = __half2float(o);
+    if (p.attn_out && rank == 0) p.attn_out[head * kHeadDim + tid] = o;
+  }
+  __syncthreads();
+
+  // ---- 4. this head's output-projection partial for rows rank*160 .. +159 ----
+  const int row0 = rank * kOutRows;
+  if (!mbar_wait(&bar_o, 0)) flag_error(FW_DEVERR_TIMEOUT);
+  if (tid < kOutRows) {
+    const uint4* wr = reinterpret_cast<const uint4*>(wout + tid * kHeadDim);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = (j + tid) & 7;  // rotation keeps the 16-byte shared loads conflict-free
+      const uint4 wv = wr[c];
+      const half2* w2 = reinterpret_cast<const half2*>(&wv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(w2[e]);
+        acc = fmaf(f.x, os[8 * c + 2 * e], acc);
+        acc = fmaf(f.y, os[8 * c + 2 * e + 1], acc);
+      }
+    }
+    __stcg(p.part + static_cast<size_t>(head) * kHidden + row0 + tid, acc);
+    __threadfence();
+  }
+
+  // ---- 5. residual update by the last CTA of this row block ----
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(p.counter + rank, 1u) == static_cast<unsigned>(heads - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid < kOutRows) {
+    const int r = row0 + tid;
+    float acc = 0.f;
+    for (int hh = 0; hh < heads; ++hh) acc += __ldcg(p.part + static_cast<size_t>(hh) * kHidden + r);
+    p.h[r] = __float2half(__half2float(hs[r]) + round_half(acc + obias));
+  }
+  if (tid == 0) p.counter[rank] = 0u;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -498,6 +824,14 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
                       &full[s], policy);
     }
   }
+  float g[5], be[5];  // final LayerNorm parameters, loaded before the wait
+  if (kLN) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      g[i] = __half2float(p.gamma[threadIdx.x + i * 256]);
+      be[i] = __half2float(p.beta[threadIdx.x + i * 256]);
+    }
+  }
   __syncthreads();
   pdl_wait();
   pdl_trigger();
@@ -509,10 +843,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
     float mean, inv;
     ln1280_stats(v, red, p.eps, mean, inv);
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const int idx = threadIdx.x + i * 256;
-      ys[idx] = __float2half(ln_apply(v[i], mean, inv, __half2float(p.gamma[idx]), __half2float(p.beta[idx])));
-    }
+    for (int i = 0; i < 5; ++i) ys[threadIdx.x + i * 256] = __float2half(ln_apply(v[i], mean, inv, g[i], be[i]));
   } else {
 #pragma unroll
     for (int i = 0; i < 5; ++i) ys[threadIdx.x + i * 256] = p.h[threadIdx.x + i * 256];
@@ -577,10 +908,10 @@ __global__ void argmax_finalize_kernel(unsigned long long* best, int64_t* tokens
 }
 
 // ---------------------------------------------------------------------------------------------
-// LayerNorm-prologue GEMV: out[r] = act(W[r] . LN(h) + b[r]) for this CTA's rows. The CTA's
-// weight rows (rows_per_cta x 1280 fp16) are bulk-copied into shared memory before the PDL wait.
-// kEmbed: h is first built from the token embedding and learned position of the current step
-// (custom/model.py:110) and CTA 0 stores it as the residual stream.
+// LayerNorm-prologue GEMV: out[r] = act(W[r] . LN(h) + b[r]) for this CTA's rows. Everything the
+// kernel reads that no in-flight launch writes is fetched before the PDL wait: the CTA's weight
+// rows (rows_per_cta x 1280 fp16) by bulk copy into shared memory, the LayerNorm gamma/beta and the
+// bias entries into registers. After the wait the only global round trip is the read of h.
 struct GemvParams {
   const half* w;
   const half* b;
@@ -593,22 +924,14 @@ struct GemvParams {
   const half* gamma;
   const half* beta;
   float eps;
-  // embedding prologue
-  const half* embed;
-  const half* pos_embed;
-  const int64_t* cur;
-  const int64_t* state;
-  const int64_t* prompt;
-  int prompt_len;
-  int vocab;
-  int max_pos;
-  half* h_out;
   // residual GEMV
   const half* x;
   half* h_res;
 };
 
-template <bool kEmbed, int kAct>
+constexpr int kGemvMaxRowsPerWarp = 4;  // rows_per_cta <= 32
+
+template <int kAct>
 __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
@@ -628,53 +951,50 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
         bulk_g2s(ws + r * kHidden, p.w + static_cast<size_t>(r0 + r) * kHidden, kHidden * 2, &bar);
     }
   }
+  float g[5], be[5], bias[kGemvMaxRowsPerWarp];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    g[i] = __half2float(p.gamma[threadIdx.x + i * 256]);
+    be[i] = __half2float(p.beta[threadIdx.x + i * 256]);
+  }
+#pragma unroll
+  for (int i = 0; i < kGemvMaxRowsPerWarp; ++i) {
+    const int r = warp + 8 * i;
+    bias[i] = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
+  }
   __syncthreads();
   pdl_wait();
   pdl_trigger();
 
   float v[5];
-  if (kEmbed) {
-    int64_t pos = p.state[0];
-    int64_t id = (pos >= 0 && pos < p.prompt_len) ? p.prompt[pos] : p.cur[0];
-    if (pos < 0 || pos >= p.max_pos || id < 0 || id >= p.vocab) {
-      if (threadIdx.x == 0 && blockIdx.x == 0) flag_error(FW_DEVERR_BAD_INDEX);
-      pos = pos < 0 ? 0 : (pos >= p.max_pos ? p.max_pos - 1 : pos);
-      id = id < 0 ? 0 : (id >= p.vocab ? p.vocab - 1 : id);
-    }
-    const half* er = p.embed + static_cast<size_t>(id) * kHidden;
-    const half* pr = p.pos_embed + static_cast<size_t>(pos) * kHidden;
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const int idx = threadIdx.x + i * 256;
-      v[i] = round_half(__half2float(er[idx]) + __half2float(pr[idx]));
-      if (blockIdx.x == 0) p.h_out[idx] = __float2half(v[i]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 5; ++i) v[i] = __half2float(p.h[threadIdx.x + i * 256]);
-  }
+  for (int i = 0; i < 5; ++i) v[i] = __half2float(p.h[threadIdx.x + i * 256]);
   float mean, inv;
   ln1280_stats(v, red, p.eps, mean, inv);
 #pragma unroll
-  for (int i = 0; i < 5; ++i) {
-    const int idx = threadIdx.x + i * 256;
-    ys[idx] = __float2half(ln_apply(v[i], mean, inv, __half2float(p.gamma[idx]), __half2float(p.beta[idx])));
-  }
+  for (int i = 0; i < 5; ++i) ys[threadIdx.x + i * 256] = __float2half(ln_apply(v[i], mean, inv, g[i], be[i]));
   __syncthreads();
   float xf[40];
   load_x40(ys, xf);
   if (nr > 0 && !mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
-  for (int r = warp; r < nr; r += 8) {
-    float acc = warp_sum(dot1280_lane(reinterpret_cast<const uint4*>(ws + r * kHidden), xf));
-    if (lane == 0) {
-      float o = round_half(acc + (p.b ? __half2float(p.b[r0 + r]) : 0.f));
-      if (kAct == 1) o = gelu_erf(o);
-      p.out[r0 + r] = __float2half(o);
+#pragma unroll
+  for (int i = 0; i < kGemvMaxRowsPerWarp; ++i) {
+    const int r = warp + 8 * i;
+    if (r < nr) {
+      const float acc = warp_sum(dot1280_lane(reinterpret_cast<const uint4*>(ws + r * kHidden), xf));
+      if (lane == 0) {
+        float o = round_half(acc + bias[i]);
+        if (kAct == 1) o = gelu_erf(o);
+        p.out[r0 + r] = __float2half(o);
+      }
     }
   }
 }
 
-// Residual GEMV: h[r] = fp16(h[r] + fp16(W[r] . x + b[r])), x of length k (multiple of 256).
+// Residual GEMV: h[r] = fp16(h[r] + fp16(W[r] . x + b[r])), x of length k (multiple of 256), one row
+// per warp (rows_per_cta == 8). The weight rows are bulk-copied and the bias and residual entries
+// loaded before the PDL wait: the previous launch must not write h (in the decode step fc2 follows
+// fc1), only x.
 __global__ void __launch_bounds__(256) gemv_residual_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
@@ -694,6 +1014,9 @@ __global__ void __launch_bounds__(256) gemv_residual_kernel(GemvParams p) {
         bulk_g2s(ws + static_cast<size_t>(r) * k, p.w + static_cast<size_t>(r0 + r) * k, k * 2, &bar);
     }
   }
+  const int r = warp;
+  const float bias = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
+  const float hres = r < nr ? __half2float(p.h_res[r0 + r]) : 0.f;
   __syncthreads();
   pdl_wait();
   pdl_trigger();
@@ -702,7 +1025,7 @@ __global__ void __launch_bounds__(256) gemv_residual_kernel(GemvParams p) {
     reinterpret_cast<uint4*>(xs)[c] = reinterpret_cast<const uint4*>(p.x)[c];
   __syncthreads();
   if (nr > 0 && !mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
-  for (int r = warp; r < nr; r += 8) {
+  if (r < nr) {
     const uint4* wr = reinterpret_cast<const uint4*>(ws + static_cast<size_t>(r) * k);
     const uint4* xr = reinterpret_cast<const uint4*>(xs);
     float acc = 0.f;
@@ -718,11 +1041,7 @@ __global__ void __launch_bounds__(256) gemv_residual_kernel(GemvParams p) {
       }
     }
     acc = warp_sum(acc);
-    if (lane == 0) {
-      const int row = r0 + r;
-      const float o = round_half(acc + (p.b ? __half2float(p.b[row]) : 0.f));
-      p.h_res[row] = __float2half(__half2float(p.h_res[row]) + o);
-    }
+    if (lane == 0) p.h_res[r0 + r] = __float2half(hres + round_half(acc + bias));
   }
 }
 
@@ -822,10 +1141,10 @@ static int rows_for(int n_out) {
   return kSmallRows;
 }
 
-template <bool kEmbed, int kAct>
+template <int kAct>
 static int launch_ln_gemv(const GemvParams& p, cudaStream_t s, bool pdl) {
   const int smem = p.rows_per_cta * kHidden * 2;
-  auto kern = ln_gemv_kernel<kEmbed, kAct>;
+  auto kern = ln_gemv_kernel<kAct>;
   cudaError_t e = ensure_smem(kern, smem);
   if (e == cudaSuccess) {
     const int grid = (p.n_out + p.rows_per_cta - 1) / p.rows_per_cta;
@@ -835,6 +1154,7 @@ static int launch_ln_gemv(const GemvParams& p, cudaStream_t s, bool pdl) {
 }
 
 static int launch_gemv_residual(const GemvParams& p, cudaStream_t s, bool pdl) {
+  if (p.rows_per_cta != kSmallRows) return set_error(FW_ERR_ARG, "gemv_residual: rows_per_cta must be %d", kSmallRows);
   const int smem = (p.rows_per_cta + 1) * p.k * 2;
   cudaError_t e = ensure_smem(gemv_residual_kernel, smem);
   if (e == cudaSuccess) {
@@ -847,6 +1167,15 @@ static int launch_gemv_residual(const GemvParams& p, cudaStream_t s, bool pdl) {
 static int launch_attention(const AttnParams& p, int heads, int splits, cudaStream_t s, bool pdl) {
   cudaError_t e = launch(attn_split_kernel, dim3(heads, splits), dim3(64), 0, s, pdl, p);
   return launch_status(e, "decode_attention");
+}
+
+template <bool kSelf, bool kEmbed>
+static int launch_head_block(const HeadBlockParams& p, int heads, cudaStream_t s, bool pdl) {
+  auto kern = head_block_kernel<kSelf, kEmbed>;
+  constexpr int smem = HeadBlockShape<kSelf>::kSmem;
+  cudaError_t e = ensure_smem(kern, smem);
+  if (e == cudaSuccess) e = launch_cluster(kern, dim3(kHeadCtas, heads), dim3(256), smem, s, pdl, kHeadCtas, p);
+  return launch_status(e, kSelf ? "self_attention_block" : "cross_attention_block");
 }
 
 template <bool kLN, bool kFinalize>
@@ -1068,7 +1397,7 @@ int fw_ln_gemv(const void* h, const void* gamma, const void* beta, float eps, co
   p.beta = static_cast<const half*>(beta);
   p.eps = eps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return act ? launch_ln_gemv<false, 1>(p, s, false) : launch_ln_gemv<false, 0>(p, s, false);
+  return act ? launch_ln_gemv<1>(p, s, false) : launch_ln_gemv<0>(p, s, false);
 }
 
 int fw_gemv_residual(const void* x, int k, const void* w, const void* b, void* h, int n_out, fw_stream_t stream) {
@@ -1092,92 +1421,75 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
   FW_REQUIRE(d->n_layers > 0 && d->n_layers <= FW_MAX_LAYERS, FW_ERR_SHAPE, "decoder_step: bad layer count");
   FW_REQUIRE(d->heads * kHeadDim == kHidden, FW_ERR_SHAPE, "decoder_step: heads * 64 must be %d", kHidden);
   FW_REQUIRE(d->max_pos > 0 && d->enc_len > 0 && d->vocab > 0, FW_ERR_SHAPE, "decoder_step: bad sizes");
-  FW_REQUIRE(d->embed && d->pos_embed && d->lm_head && d->final_g && d->final_b && d->h && d->qkv && d->attn &&
-                 d->cq && d->ffn && d->part_m && d->part_l && d->part_acc && d->counters && d->cur && d->state &&
-                 d->tokens && d->best,
+  FW_REQUIRE(d->embed && d->pos_embed && d->lm_head && d->final_g && d->final_b && d->h && d->ffn && d->part_acc &&
+                 d->counters && d->cur && d->state && d->tokens && d->best,
              FW_ERR_NULL, "decoder_step: a required pointer is NULL");
   FW_REQUIRE(d->prompt_len == 0 || d->prompt != nullptr, FW_ERR_NULL, "decoder_step: prompt is NULL");
   const int self_splits = (d->max_pos + kSplitKeys - 1) / kSplitKeys;
   const int cross_splits = (d->enc_len + kSplitKeys - 1) / kSplitKeys;
-  FW_REQUIRE(self_splits <= kMaxSplits && cross_splits <= kMaxSplits, FW_ERR_SHAPE,
-             "decoder_step: max_pos and enc_len must be <= %d", kMaxSplits * kSplitKeys);
-  FW_REQUIRE(d->ws_splits >= self_splits && d->ws_splits >= cross_splits, FW_ERR_SHAPE,
-             "decoder_step: workspace too small for %d splits", cross_splits);
+  FW_REQUIRE(self_splits <= kHeadCtas && cross_splits <= kHeadCtas * kHeadMaxUnits, FW_ERR_SHAPE,
+             "decoder_step: max_pos must be <= %d and enc_len <= %d", kHeadCtas * kSplitKeys,
+             kHeadCtas * kHeadMaxUnits * kSplitKeys);
+  FW_REQUIRE(d->ws_splits * kHeadDim >= kHidden, FW_ERR_SHAPE,
+             "decoder_step: part_acc must hold heads * 1280 floats (ws_splits >= %d)", kHidden / kHeadDim);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (steps <= 0) return FW_OK;
   half* h = static_cast<half*>(d->h);
-  half* qkv = static_cast<half*>(d->qkv);
-  half* attn = static_cast<half*>(d->attn);
-  half* cq = static_cast<half*>(d->cq);
   half* ffn = static_cast<half*>(d->ffn);
   for (int step = 0; step < steps; ++step) {
     for (int l = 0; l < d->n_layers; ++l) {
       const fw_decoder_layer_t& L = d->layers[l];
-      // LN1 + QKV (+ embedding on layer 0)
-      GemvParams g{};
-      g.w = static_cast<const half*>(L.qkv_w);
-      g.b = static_cast<const half*>(L.qkv_b);
-      g.out = qkv;
-      g.n_out = 3 * kHidden;
-      g.k = kHidden;
-      g.rows_per_cta = kQkvRows;
-      g.h = h;
-      g.gamma = static_cast<const half*>(L.ln1_g);
-      g.beta = static_cast<const half*>(L.ln1_b);
-      g.eps = d->eps;
       int rc;
-      if (l == 0) {
-        g.embed = static_cast<const half*>(d->embed);
-        g.pos_embed = static_cast<const half*>(d->pos_embed);
-        g.cur = d->cur;
-        g.state = d->state;
-        g.prompt = d->prompt;
-        g.prompt_len = d->prompt_len;
-        g.vocab = d->vocab;
-        g.max_pos = d->max_pos;
-        g.h_out = h;
-        rc = launch_ln_gemv<true, 0>(g, s, true);
-      } else {
-        rc = launch_ln_gemv<false, 0>(g, s, true);
-      }
+      // LN1 + q/k/v (+ embedding on layer 0) + self attention with the cache write + out_proj + residual
+      HeadBlockParams a{};
+      a.h = h;
+      a.gamma = static_cast<const half*>(L.ln1_g);
+      a.beta = static_cast<const half*>(L.ln1_b);
+      a.eps = d->eps;
+      a.embed = static_cast<const half*>(d->embed);
+      a.pos_embed = static_cast<const half*>(d->pos_embed);
+      a.cur = d->cur;
+      a.prompt = d->prompt;
+      a.prompt_len = d->prompt_len;
+      a.vocab = d->vocab;
+      a.state = d->state;
+      a.max_pos = d->max_pos;
+      a.state_early = l > 0;  // on layer 0 the previous launch (LM head) advances the position
+      a.w = static_cast<const half*>(L.qkv_w);
+      a.b = static_cast<const half*>(L.qkv_b);
+      a.k = static_cast<half*>(L.self_k);
+      a.v = static_cast<half*>(L.self_v);
+      a.kv_len = d->max_pos;
+      a.scale = d->scale;
+      a.wo = static_cast<const half*>(L.out_w);
+      a.bo = static_cast<const half*>(L.out_b);
+      a.part = d->part_acc;
+      a.counter = d->counters;
+      a.attn_out = static_cast<half*>(d->attn);
+      rc = l == 0 ? launch_head_block<true, true>(a, d->heads, s, true)
+                  : launch_head_block<true, false>(a, d->heads, s, true);
       if (rc) return rc;
-      // self attention with the fused cache write
-      AttnParams a{qkv, static_cast<half*>(L.self_k), static_cast<half*>(L.self_v), qkv + kHidden, qkv + 2 * kHidden,
-                   d->state, d->max_pos, d->scale, d->part_m, d->part_l, d->part_acc, attn, d->counters};
-      if ((rc = launch_attention(a, d->heads, self_splits, s, true))) return rc;
-      // out projection + residual
-      GemvParams r{};
-      r.w = static_cast<const half*>(L.out_w);
-      r.b = static_cast<const half*>(L.out_b);
-      r.n_out = kHidden;
-      r.k = kHidden;
-      r.rows_per_cta = kSmallRows;
-      r.x = attn;
-      r.h_res = h;
-      if ((rc = launch_gemv_residual(r, s, true))) return rc;
-      // LN2 + cross q
-      g = GemvParams{};
-      g.w = static_cast<const half*>(L.cq_w);
-      g.b = static_cast<const half*>(L.cq_b);
-      g.out = cq;
-      g.n_out = kHidden;
-      g.k = kHidden;
-      g.rows_per_cta = kSmallRows;
-      g.h = h;
-      g.gamma = static_cast<const half*>(L.ln2_g);
-      g.beta = static_cast<const half*>(L.ln2_b);
-      g.eps = d->eps;
-      if ((rc = launch_ln_gemv<false, 0>(g, s, true))) return rc;
-      // cross attention over the encoder states
-      AttnParams c{cq, const_cast<half*>(static_cast<const half*>(L.cross_k)),
-                   const_cast<half*>(static_cast<const half*>(L.cross_v)), nullptr, nullptr, nullptr, d->enc_len,
-                   d->scale, d->part_m, d->part_l, d->part_acc, attn, d->counters};
-      if ((rc = launch_attention(c, d->heads, cross_splits, s, true))) return rc;
-      r.w = static_cast<const half*>(L.co_w);
-      r.b = static_cast<const half*>(L.co_b);
-      if ((rc = launch_gemv_residual(r, s, true))) return rc;
+      // LN2 + cross q + cross attention + cross out_proj + residual
+      HeadBlockParams c{};
+      c.h = h;
+      c.gamma = static_cast<const half*>(L.ln2_g);
+      c.beta = static_cast<const half*>(L.ln2_b);
+      c.eps = d->eps;
+      c.state = d->state;
+      c.max_pos = d->max_pos;
+      c.w = static_cast<const half*>(L.cq_w);
+      c.b = static_cast<const half*>(L.cq_b);
+      c.k = const_cast<half*>(static_cast<const half*>(L.cross_k));
+      c.v = const_cast<half*>(static_cast<const half*>(L.cross_v));
+      c.kv_len = d->enc_len;
+      c.scale = d->scale;
+      c.wo = static_cast<const half*>(L.co_w);
+      c.bo = static_cast<const half*>(L.co_b);
+      c.part = d->part_acc;
+      c.counter = d->counters;
+      if ((rc = launch_head_block<false, false>(c, d->heads, s, true))) return rc;
       // LN3 + fc1 + GELU
-      g = GemvParams{};
+      GemvParams g{};
       g.w = static_cast<const half*>(L.fc1_w);
       g.b = static_cast<const half*>(L.fc1_b);
       g.out = ffn;
@@ -1188,9 +1500,9 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
       g.gamma = static_cast<const half*>(L.ln3_g);
       g.beta = static_cast<const half*>(L.ln3_b);
       g.eps = d->eps;
-      if ((rc = launch_ln_gemv<false, 1>(g, s, true))) return rc;
+      if ((rc = launch_ln_gemv<1>(g, s, true))) return rc;
       // fc2 + residual
-      r = GemvParams{};
+      GemvParams r{};
       r.w = static_cast<const half*>(L.fc2_w);
       r.b = static_cast<const half*>(L.fc2_b);
       r.n_out = kHidden;

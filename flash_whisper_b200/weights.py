@@ -162,9 +162,14 @@ def load_hf_model(state_dict, dims=TURBO, dtype=torch.float32):
 
 
 def pack_decoder(sd, dims=TURBO, device='cuda', dtype=torch.float16):
-    """Decoder weights in kernel layout (fp16 on `device`)."""
+    """Decoder weights in kernel layout (fp16 on `device`). The attention output projections are
+    head-major [heads, d_model, head_dim]: the slice of head h, W[:, h*64:(h+1)*64], is contiguous,
+    so the per-head attention block streams it with one bulk copy."""
     def t(name):
         return sd[name].to(device=device, dtype=dtype).contiguous()
+
+    def head_major(w):
+        return w.view(w.size(0), dims.heads, dims.head_dim).permute(1, 0, 2).contiguous()
 
     layers = []
     for i in range(dims.decoder_layers):
@@ -177,9 +182,9 @@ def pack_decoder(sd, dims=TURBO, device='cuda', dtype=torch.float16):
             qkv_w=torch.cat([t(f'{p}.self_attn.q_proj.weight'), t(f'{p}.self_attn.k_proj.weight'),
                              t(f'{p}.self_attn.v_proj.weight')]).contiguous(),
             qkv_b=torch.cat([t(f'{p}.self_attn.q_proj.bias'), zeros, t(f'{p}.self_attn.v_proj.bias')]).contiguous(),
-            out=(t(f'{p}.self_attn.out_proj.weight'), t(f'{p}.self_attn.out_proj.bias')),
+            out=(head_major(t(f'{p}.self_attn.out_proj.weight')), t(f'{p}.self_attn.out_proj.bias')),
             cross_q=(t(f'{p}.encoder_attn.q_proj.weight'), t(f'{p}.encoder_attn.q_proj.bias')),
-            cross_out=(t(f'{p}.encoder_attn.out_proj.weight'), t(f'{p}.encoder_attn.out_proj.bias')),
+            cross_out=(head_major(t(f'{p}.encoder_attn.out_proj.weight')), t(f'{p}.encoder_attn.out_proj.bias')),
             fc1=(t(f'{p}.fc1.weight'), t(f'{p}.fc1.bias')),
             fc2=(t(f'{p}.fc2.weight'), t(f'{p}.fc2.bias'))))
     cross_w = torch.cat([torch.cat([t(f'model.decoder.layers.{i}.encoder_attn.k_proj.weight'),

@@ -128,16 +128,19 @@ int fw_ln_gemv(const void* h, const void* gamma, const void* beta, float eps, co
 int fw_gemv_residual(const void* x, int k, const void* w, const void* b, void* h, int n_out, fw_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
- * Whole decode step (custom/model.py:107-123) as 34 PDL-chained launches.
+ * Whole decode step (custom/model.py:107-123) as 17 PDL-chained launches: per layer a self-attention
+ * block and a cross-attention block (one thread-block cluster per head: LN, projection, split-K
+ * attention, output projection and residual in one launch), fc1 and fc2; then the LM head.
  * ---------------------------------------------------------------------------------------- */
 #define FW_MAX_LAYERS 8
 
 typedef struct {
   const void *ln1_g, *ln1_b, *ln2_g, *ln2_b, *ln3_g, *ln3_b; /* [1280] */
   const void *qkv_w, *qkv_b;                                 /* [3840,1280], [3840] (K bias zero) */
-  const void *out_w, *out_b;                                 /* [1280,1280], [1280] */
-  const void *cq_w, *cq_b;                                   /* cross q_proj */
-  const void *co_w, *co_b;                                   /* cross out_proj */
+  const void *out_w, *out_b;   /* out_proj, HEAD-MAJOR [heads, 1280, 64] = W.view(1280, heads, 64)
+                                  .permute(1, 0, 2); [1280] */
+  const void *cq_w, *cq_b;     /* cross q_proj [1280,1280], [1280] */
+  const void *co_w, *co_b;     /* cross out_proj, head-major like out_w */
   const void *fc1_w, *fc1_b;                                 /* [5120,1280], [5120] */
   const void *fc2_w, *fc2_b;                                 /* [1280,5120], [1280] */
   void *self_k, *self_v;                                     /* [heads, max_pos, 64] */
@@ -152,9 +155,11 @@ typedef struct {
   const bool *base_mask, *first_mask;      /* [vocab]; first_mask applies to the last prompt step */
   const int64_t* prompt;                   /* [prompt_len] forced input ids (may be NULL if 0) */
   fw_decoder_layer_t layers[FW_MAX_LAYERS];
-  void *h, *qkv, *attn, *cq, *ffn;          /* fp16 [1280], [3840], [1280], [1280], [5120] */
-  float *part_m, *part_l, *part_acc;        /* attention split scratch */
-  int64_t ws_splits;                        /* capacity of part_m/part_l in splits per head */
+  void *h, *qkv, *attn, *cq, *ffn;          /* fp16 [1280] residual, -, [1280] attention output of the
+                                               last self block (may be NULL), -, [5120] fc1 output */
+  float *part_m, *part_l, *part_acc;        /* part_acc: fp32 [heads * ws_splits * 64] scratch (per-head
+                                               output-projection partials); part_m, part_l unused */
+  int64_t ws_splits;                        /* >= 20 (part_acc holds heads * 1280 floats) */
   unsigned int* counters;                   /* [heads + 1], zero before the first step; left zero */
   int64_t *cur, *state, *tokens, *best;     /* [1], [2] = {position, count}, [n_tokens], [1] (0) */
   int64_t n_tokens;
