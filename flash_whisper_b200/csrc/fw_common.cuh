@@ -143,6 +143,12 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// Requests `bytes` (multiple of 16, 16-byte aligned address) from global memory into L2 without
+// waiting, so a later bulk copy of the same range hits L2.
+__device__ __forceinline__ void l2_prefetch(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Split cluster barrier: every thread of every CTA of the cluster arrives, then waits. A CTA may
 // access another CTA's shared memory only after a completed barrier phase that the other CTA
 // arrived at (so it is known to be running), and must not exit while others may still access its

@@ -100,6 +100,39 @@ __device__ __forceinline__ float dot1280_lane(const uint4* row, const float (&xf
   return acc;
 }
 
+// kRows dot products of 1280-wide fp16 rows `stride` elements apart with x (as dot1280_lane), their
+// loads and fma chains interleaved, followed by the warp xor-tree of each: every result is
+// bit-identical to warp_sum(dot1280_lane(row, xf)), only the latency overlaps.
+template <int kRows>
+__device__ __forceinline__ void dot1280_rows(const half* row0, int stride, const float (&xf)[40], float (&out)[kRows]) {
+  const int lane = threadIdx.x & 31;
+  float acc[kRows];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+    uint4 wv[kRows];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) wv[r] = reinterpret_cast<const uint4*>(row0 + r * stride)[lane + 32 * c];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const half2* p = reinterpret_cast<const half2*>(&wv[r]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(p[k]);
+        acc[r] = fmaf(f.x, xf[c * 8 + 2 * k], acc[r]);
+        acc[r] = fmaf(f.y, xf[c * 8 + 2 * k + 1], acc[r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) out[r] = acc[r];
+}
+
 __device__ __forceinline__ void load_x40(const half* xs, float (&xf)[40]) {
   const int lane = threadIdx.x & 31;
   const uint4* x4 = reinterpret_cast<const uint4*>(xs);
@@ -465,6 +498,7 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
 // Weight rows, the K/V splits and the output-projection slice (head-major [heads, 1280, 64]) are
 // bulk-copied into shared memory before griddepcontrol.wait. Only two cluster barriers are needed,
 // after which no CTA touches another CTA's shared memory.
+constexpr int kHeads = kHidden / kHeadDim;                // 20
 constexpr int kHeadCtas = 8;                              // CTAs per head cluster
 constexpr int kHeadMaxUnits = 3;                          // attention splits per CTA (cross: 24 / 8)
 constexpr int kOutRows = kHidden / kHeadCtas;             // output-projection rows per CTA (160)
@@ -510,7 +544,9 @@ struct HeadBlockShape {
   static constexpr int kProjBytes = kProjRows * kHidden * 2;
   static constexpr int kKvBytes = kUnits * 2 * kSplitKeys * kHeadDim * 2;
   static constexpr int kOutBytes = kOutRows * kHeadDim * 2;
-  static constexpr int kSmem = kProjBytes + kKvBytes + kOutBytes;
+  // the output-projection slice reuses the projection rows' buffer once step 1 is done
+  static constexpr int kWBytes = kProjBytes > kOutBytes ? kProjBytes : kOutBytes;
+  static constexpr int kSmem = kWBytes + kKvBytes;
 };
 
 template <bool kSelf, bool kEmbed>
@@ -527,6 +563,7 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   __shared__ float sm_m[S::kSlots];
   __shared__ float sm_l[S::kSlots];
   __shared__ __align__(16) float sm_acc[S::kSlots][kHeadDim];
+  __shared__ float sm_w[S::kSlots];
   __shared__ int s_last;
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -535,8 +572,8 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   const int heads = gridDim.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   half* wproj = reinterpret_cast<half*>(smem);
-  half* kvs = reinterpret_cast<half*>(smem + S::kProjBytes);
-  half* wout = reinterpret_cast<half*>(smem + S::kProjBytes + S::kKvBytes);
+  half* kvs = reinterpret_cast<half*>(smem + S::kWBytes);
+  half* wout = wproj;  // reused after step 1
   const int splits = (p.kv_len + kSplitKeys - 1) / kSplitKeys;
   half* kh = p.k + static_cast<size_t>(head) * p.kv_len * kHeadDim;
   half* vh = p.v + static_cast<size_t>(head) * p.kv_len * kHeadDim;
@@ -586,8 +623,8 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
                  &bar_kv);
       }
     }
-    mbar_arrive_expect_tx(&bar_o, S::kOutBytes);
-    bulk_g2s(wout, p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes, &bar_o);
+    // the output-projection slice is copied into shared memory after step 1; warm it in L2 now
+    l2_prefetch(p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes);
   }
   // LayerNorm parameters and biases are weights: loaded before the wait, into registers
   constexpr int kRowsPerWarp = (S::kProjRows + 7) / 8;
@@ -644,16 +681,21 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     load_x40(ys, xf);
     if (!mbar_wait(&bar_w, 0)) flag_error(FW_DEVERR_TIMEOUT);
     cluster_wait();
+    static_assert(S::kProjRows % 8 == 0, "projection rows must fill the 8 warps evenly");
+    float acc[kRowsPerWarp];
+    dot1280_rows<kRowsPerWarp>(wproj + warp * kHidden, 8 * kHidden, xf, acc);
+    if (lane < kHeadCtas) {  // every lane holds the same sums; lane r stores into cluster rank r
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-      const int r = warp + 8 * i;
-      if (r >= S::kProjRows) break;
-      const float acc = warp_sum(dot1280_lane(reinterpret_cast<const uint4*>(wproj + r * kHidden), xf));
-      if (lane < kHeadCtas)  // every lane holds the same sum; lane r stores into cluster rank r
-        *cluster.map_shared_rank(&qv[rank * S::kProjRows + r], lane) = __float2half(acc + pbias[i]);
+      for (int i = 0; i < kRowsPerWarp; ++i)
+        *cluster.map_shared_rank(&qv[rank * S::kProjRows + warp + 8 * i], lane) = __float2half(acc[i] + pbias[i]);
     }
   }
   cluster.sync();  // q (| k | v) of this head visible in every CTA
+  if (tid == 0) {  // every thread of this CTA is past its reads of the projection rows
+    fence_proxy_async_shared();
+    mbar_arrive_expect_tx(&bar_o, S::kOutBytes);
+    bulk_g2s(wout, p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes, &bar_o);
+  }
 
   // ---- 2. attention splits ----
   {
@@ -694,14 +736,19 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   }
   cluster.sync();  // every split's partial visible in every CTA; no DSMEM access after this point
 
-  // ---- 3. split combine (whisper_kernels.cu:193-213 order), in every CTA ----
-  if (tid < kHeadDim) {
+  // ---- 3. split combine (whisper_kernels.cu:193-213 order), in every CTA: the split weights
+  // exp(m_s - m) are computed one per thread, then the sums run in split order ----
+  if (tid < splits) {
     float m = -INFINITY;
     for (int s = 0; s < splits; ++s) m = fmaxf(m, sm_m[s]);
+    sm_w[tid] = sm_l[tid] > 0.f ? __expf(sm_m[tid] - m) : 0.f;
+  }
+  __syncthreads();
+  if (tid < kHeadDim) {
     float num = 0.f, den = 0.f;
     for (int s = 0; s < splits; ++s) {
       if (sm_l[s] > 0.f) {
-        const float w = __expf(sm_m[s] - m);
+        const float w = sm_w[s];
         num = fmaf(sm_acc[s][tid], w, num);
         den = fmaf(sm_l[s], w, den);
       }
@@ -731,19 +778,27 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
       }
     }
     __stcg(p.part + static_cast<size_t>(head) * kHidden + row0 + tid, acc);
-    __threadfence();
   }
 
   // ---- 5. residual update by the last CTA of this row block ----
+  // Release/acquire through thread 0 (the barrier orders the CTA's partial stores before its fence).
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(p.counter + rank, 1u) == static_cast<unsigned>(heads - 1);
+  if (tid == 0) {
+    __threadfence();
+    const bool last = atomicAdd(p.counter + rank, 1u) == static_cast<unsigned>(heads - 1);
+    if (last) __threadfence();
+    s_last = last;
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   if (tid < kOutRows) {
     const int r = row0 + tid;
+    float pv[kHeads];
+#pragma unroll
+    for (int hh = 0; hh < kHeads; ++hh) pv[hh] = __ldcg(p.part + static_cast<size_t>(hh) * kHidden + r);
     float acc = 0.f;
-    for (int hh = 0; hh < heads; ++hh) acc += __ldcg(p.part + static_cast<size_t>(hh) * kHidden + r);
+#pragma unroll
+    for (int hh = 0; hh < kHeads; ++hh) acc += pv[hh];
     p.h[r] = __float2half(__half2float(hs[r]) + round_half(acc + obias));
   }
   if (tid == 0) p.counter[rank] = 0u;
@@ -751,13 +806,17 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
 
 // ---------------------------------------------------------------------------------------------
 // LM head: fused (optional final LayerNorm) + GEMV over the vocab + argmax (+ optional finalize).
-// One CTA per SM owns a contiguous range of vocab rows and streams them through a ring of
-// kLmStages shared-memory stages (8 rows each, one row per warp) fed by bulk async copies; the
-// first stages are requested before griddepcontrol.wait.
-constexpr int kLmStages = 6;
-constexpr int kLmRows = 8;
-constexpr int kLmStageBytes = kLmRows * kHidden * 2;
-constexpr int kLmSmem = kLmStages * kLmStageBytes;
+// One CTA per SM owns a contiguous range of vocab rows; each of its 8 warps streams its own
+// contiguous share through a private ring of kLmSlots shared-memory slots (kLmSlotRows rows each)
+// fed by bulk async copies issued by the warp's lane 0. Warps never wait for one another inside the
+// loop, so a slot is refilled as soon as its warp has consumed it and the bytes in flight stay high
+// while other warps compute; two rows per slot are dotted together to overlap their latency. The
+// first slots are requested before griddepcontrol.wait.
+constexpr int kLmSlots = 2;
+constexpr int kLmSlotRows = 2;
+constexpr int kLmSlotBytes = kLmSlotRows * kHidden * 2;
+constexpr int kLmSmem = 8 * kLmSlots * kLmSlotBytes;
+constexpr int kLmMaxRowsPerCta = 512;  // vocab <= 512 * SMs
 
 struct LmParams {
   const half* h;
@@ -802,27 +861,39 @@ __device__ __forceinline__ void finalize_token(unsigned long long b, int64_t* to
 template <bool kLN, bool kFinalize>
 __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[kLmStages];
+  __shared__ __align__(8) uint64_t full[8][kLmSlots];
   __shared__ float red[16];
   __shared__ __align__(16) half ys[kHidden];
   __shared__ unsigned long long warp_best[8];
+  __shared__ uint8_t msk[2][kLmMaxRowsPerCta];  // suppress flags of this CTA's rows: base, first step
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int r1 = min(p.vocab, r0 + p.rows_per_cta);
   const int nrows = max(0, r1 - r0);
-  const int nst = (nrows + kLmRows - 1) / kLmRows;
+  // this warp's rows
+  const int per_warp = (nrows + 7) / 8;
+  const int w0 = r0 + warp * per_warp;
+  const int wn = max(0, min(r1, w0 + per_warp) - w0);
+  const int nst = (wn + kLmSlotRows - 1) / kLmSlotRows;
+  uint8_t* ring = smem + warp * kLmSlots * kLmSlotBytes;
   const uint64_t policy = policy_evict_first();
+  auto issue = [&](int st, int slot) {
+    const int rows = min(kLmSlotRows, wn - st * kLmSlotRows);
+    const unsigned bytes = static_cast<unsigned>(rows) * kHidden * 2;
+    mbar_arrive_expect_tx(&full[warp][slot], bytes);
+    bulk_g2s_stream(ring + slot * kLmSlotBytes, p.w + static_cast<size_t>(w0 + st * kLmSlotRows) * kHidden, bytes,
+                    &full[warp][slot], policy);
+  };
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kLmStages; ++s) mbar_init(&full[s], 1);
+  if (lane == 0) {
+    for (int s = 0; s < kLmSlots; ++s) mbar_init(&full[warp][s], 1);
     mbar_fence_init();
-    for (int s = 0; s < kLmStages && s < nst; ++s) {
-      const int rows = min(kLmRows, nrows - s * kLmRows);
-      const unsigned bytes = static_cast<unsigned>(rows) * kHidden * 2;
-      mbar_arrive_expect_tx(&full[s], bytes);
-      bulk_g2s_stream(smem + s * kLmStageBytes, p.w + static_cast<size_t>(r0 + s * kLmRows) * kHidden, bytes,
-                      &full[s], policy);
-    }
+    for (int s = 0; s < kLmSlots && s < nst; ++s) issue(s, s);
+  }
+  // The suppress masks are constant: staged before the wait so the row loop reads shared memory.
+  for (int i = threadIdx.x; i < nrows; i += 256) {
+    msk[0][i] = p.mask ? static_cast<uint8_t>(p.mask[r0 + i]) : 0;
+    msk[1][i] = p.first_mask ? static_cast<uint8_t>(p.first_mask[r0 + i]) : 0;
   }
   float g[5], be[5];  // final LayerNorm parameters, loaded before the wait
   if (kLN) {
@@ -852,32 +923,37 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
   float xf[40];
   load_x40(ys, xf);
 
-  const bool* mask = p.mask;
-  if (kFinalize && p.first_mask && p.prompt_len > 0 && p.state[0] == p.prompt_len - 1) mask = p.first_mask;
+  const uint8_t* mask = msk[0];
+  if (kFinalize && p.first_mask && p.prompt_len > 0 && p.state[0] == p.prompt_len - 1) mask = msk[1];
 
   unsigned long long mine = 0;
+  auto take = [&](float acc, int row) {  // logits are fp16 in the reference (whisper_kernels.cu:70-71)
+    if (!mask[row - r0]) {
+      const unsigned long long key = pack_score(round_half(acc), row);
+      mine = key > mine ? key : mine;
+    }
+  };
   for (int s = 0; s < nst; ++s) {
-    const int slotb = s % kLmStages;
-    if (!mbar_wait(&full[slotb], (s / kLmStages) & 1)) flag_error(FW_DEVERR_TIMEOUT);
-    const int row = r0 + s * kLmRows + warp;
-    if (row < r1) {
-      const uint4* wr = reinterpret_cast<const uint4*>(smem + slotb * kLmStageBytes + warp * kHidden * 2);
-      float acc = warp_sum(dot1280_lane(wr, xf));
-      acc = round_half(acc);  // logits are fp16 in the reference (whisper_kernels.cu:70-71)
-      if (lane == 0 && !(mask && mask[row])) {
-        const unsigned long long key = pack_score(acc, row);
-        mine = key > mine ? key : mine;
+    const int slot = s % kLmSlots;
+    if (!mbar_wait(&full[warp][slot], (s / kLmSlots) & 1)) flag_error(FW_DEVERR_TIMEOUT);
+    const int row = w0 + s * kLmSlotRows;
+    const half* base = reinterpret_cast<const half*>(ring + slot * kLmSlotBytes);
+    if (row + kLmSlotRows <= w0 + wn) {
+      float acc[kLmSlotRows];
+      dot1280_rows<kLmSlotRows>(base, kHidden, xf, acc);
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < kLmSlotRows; ++i) take(acc[i], row + i);
+      }
+    } else {
+      for (int i = 0; row + i < w0 + wn; ++i) {
+        float acc[1];
+        dot1280_rows<1>(base + i * kHidden, kHidden, xf, acc);
+        if (lane == 0) take(acc[0], row + i);
       }
     }
-    __syncthreads();
-    if (threadIdx.x == 0 && s + kLmStages < nst) {
-      const int sn = s + kLmStages;
-      const int rows = min(kLmRows, nrows - sn * kLmRows);
-      const unsigned bytes = static_cast<unsigned>(rows) * kHidden * 2;
-      mbar_arrive_expect_tx(&full[slotb], bytes);
-      bulk_g2s_stream(smem + slotb * kLmStageBytes, p.w + static_cast<size_t>(r0 + sn * kLmRows) * kHidden, bytes,
-                      &full[slotb], policy);
-    }
+    __syncwarp();  // every lane is done reading the slot before it is refilled
+    if (lane == 0 && s + kLmSlots < nst) issue(s + kLmSlots, slot);
   }
   if (lane == 0) warp_best[warp] = mine;
   __syncthreads();
@@ -929,9 +1005,8 @@ struct GemvParams {
   half* h_res;
 };
 
-constexpr int kGemvMaxRowsPerWarp = 4;  // rows_per_cta <= 32
-
-template <int kAct>
+// kRowsPerWarp = rows_per_cta / 8 (1, 3 or 4): warp w owns rows w, w + 8, ...
+template <int kAct, int kRowsPerWarp>
 __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
@@ -951,14 +1026,14 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
         bulk_g2s(ws + r * kHidden, p.w + static_cast<size_t>(r0 + r) * kHidden, kHidden * 2, &bar);
     }
   }
-  float g[5], be[5], bias[kGemvMaxRowsPerWarp];
+  float g[5], be[5], bias[kRowsPerWarp];
 #pragma unroll
   for (int i = 0; i < 5; ++i) {
     g[i] = __half2float(p.gamma[threadIdx.x + i * 256]);
     be[i] = __half2float(p.beta[threadIdx.x + i * 256]);
   }
 #pragma unroll
-  for (int i = 0; i < kGemvMaxRowsPerWarp; ++i) {
+  for (int i = 0; i < kRowsPerWarp; ++i) {
     const int r = warp + 8 * i;
     bias[i] = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
   }
@@ -977,71 +1052,118 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
   float xf[40];
   load_x40(ys, xf);
   if (nr > 0 && !mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
+  if (nr == 8 * kRowsPerWarp) {  // full CTA: all rows interleaved
+    float acc[kRowsPerWarp];
+    dot1280_rows<kRowsPerWarp>(ws + warp * kHidden, 8 * kHidden, xf, acc);
+    if (lane < kRowsPerWarp) {  // lane i finishes row warp + 8 i
+      float a = acc[0], bi = bias[0];
 #pragma unroll
-  for (int i = 0; i < kGemvMaxRowsPerWarp; ++i) {
-    const int r = warp + 8 * i;
-    if (r < nr) {
-      const float acc = warp_sum(dot1280_lane(reinterpret_cast<const uint4*>(ws + r * kHidden), xf));
-      if (lane == 0) {
-        float o = round_half(acc + bias[i]);
-        if (kAct == 1) o = gelu_erf(o);
-        p.out[r0 + r] = __float2half(o);
+      for (int i = 1; i < kRowsPerWarp; ++i)
+        if (lane == i) {
+          a = acc[i];
+          bi = bias[i];
+        }
+      float o = round_half(a + bi);
+      if (kAct == 1) o = gelu_erf(o);
+      p.out[r0 + warp + 8 * lane] = __float2half(o);
+    }
+  } else {  // ragged last CTA
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const int r = warp + 8 * i;
+      if (r < nr) {
+        const float acc = warp_sum(dot1280_lane(reinterpret_cast<const uint4*>(ws + r * kHidden), xf));
+        if (lane == 0) {
+          float o = round_half(acc + bias[i]);
+          if (kAct == 1) o = gelu_erf(o);
+          p.out[r0 + r] = __float2half(o);
+        }
       }
     }
   }
 }
 
-// Residual GEMV: h[r] = fp16(h[r] + fp16(W[r] . x + b[r])), x of length k (multiple of 256), one row
-// per warp (rows_per_cta == 8). The weight rows are bulk-copied and the bias and residual entries
-// loaded before the PDL wait: the previous launch must not write h (in the decode step fc2 follows
-// fc1), only x.
-__global__ void __launch_bounds__(256) gemv_residual_kernel(GemvParams p) {
+// Residual GEMV: h[r] = fp16(h[r] + fp16(W[r] . x + b[r])) for this CTA's kResidRows rows, x of
+// length k = 256 * kChunks. The CTA splits k, not rows: thread t owns 16-byte chunks t, t + 320, ...
+// of x (in registers) and of every row, accumulates one partial per row, and the partials are summed
+// over each warp (xor tree) and then over the warps in order, so each weight and x byte is read
+// from shared memory once. The weight rows are bulk-copied and the bias and residual entries loaded
+// before the PDL wait: the previous launch must not write h (in the decode step fc2 follows fc1).
+constexpr int kResidRows = 10;  // 1280 / 10 = 128 CTAs: no SM holds two, leaving room for the next launch
+constexpr int kResidThreads = 320;
+
+template <int kChunks>
+__global__ void __launch_bounds__(kResidThreads) gemv_residual_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r0 = blockIdx.x * p.rows_per_cta;
-  const int nr = min(p.rows_per_cta, p.n_out - r0);
-  const int k = p.k;
-  half* ws = reinterpret_cast<half*>(smem);
-  half* xs = ws + static_cast<size_t>(p.rows_per_cta) * k;
+  __shared__ float red[kResidThreads / 32][kResidRows];
+  constexpr int k = 256 * kChunks;
+  constexpr int kc = k / 8;                                            // 16-byte chunks per row
+  constexpr int kPer = (kc + kResidThreads - 1) / kResidThreads;       // chunks per thread
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = blockIdx.x * kResidRows;
+  const int nr = min(kResidRows, p.n_out - r0);
+  const uint4* ws = reinterpret_cast<const uint4*>(smem);
 
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     mbar_init(&bar, 1);
     mbar_fence_init();
     if (nr > 0) {
       mbar_arrive_expect_tx(&bar, static_cast<unsigned>(nr) * k * 2);
       for (int r = 0; r < nr; ++r)
-        bulk_g2s(ws + static_cast<size_t>(r) * k, p.w + static_cast<size_t>(r0 + r) * k, k * 2, &bar);
+        bulk_g2s(smem + static_cast<size_t>(r) * k * 2, p.w + static_cast<size_t>(r0 + r) * k, k * 2, &bar);
     }
   }
-  const int r = warp;
-  const float bias = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
-  const float hres = r < nr ? __half2float(p.h_res[r0 + r]) : 0.f;
+  const bool owner = tid < nr;  // thread r finishes row r
+  const float bias = (p.b && owner) ? __half2float(p.b[r0 + tid]) : 0.f;
+  const float hres = owner ? __half2float(p.h_res[r0 + tid]) : 0.f;
   __syncthreads();
   pdl_wait();
   pdl_trigger();
-  const int kc = k / 8;  // 16-byte chunks
-  for (int c = threadIdx.x; c < kc; c += 256)
-    reinterpret_cast<uint4*>(xs)[c] = reinterpret_cast<const uint4*>(p.x)[c];
-  __syncthreads();
-  if (nr > 0 && !mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
-  if (r < nr) {
-    const uint4* wr = reinterpret_cast<const uint4*>(ws + static_cast<size_t>(r) * k);
-    const uint4* xr = reinterpret_cast<const uint4*>(xs);
-    float acc = 0.f;
-    for (int c = lane; c < kc; c += 32) {
-      const uint4 wv = wr[c], xv = xr[c];
-      const half2* pw = reinterpret_cast<const half2*>(&wv);
-      const half2* px = reinterpret_cast<const half2*>(&xv);
+  uint4 xv[kPer];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 fw = __half22float2(pw[j]), fx = __half22float2(px[j]);
-        acc = fmaf(fw.x, fx.x, acc);
-        acc = fmaf(fw.y, fx.y, acc);
+  for (int j = 0; j < kPer; ++j) {
+    const int c = tid + kResidThreads * j;
+    xv[j] = c < kc ? reinterpret_cast<const uint4*>(p.x)[c] : make_uint4(0, 0, 0, 0);
+  }
+  if (nr > 0 && !mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
+  float acc[kResidRows];
+#pragma unroll
+  for (int r = 0; r < kResidRows; ++r) acc[r] = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int c = tid + kResidThreads * j;
+    if (c < kc) {
+      const half2* px = reinterpret_cast<const half2*>(&xv[j]);
+#pragma unroll
+      for (int r = 0; r < kResidRows; ++r) {
+        if (r < nr) {
+          const uint4 wv = ws[r * kc + c];
+          const half2* pw = reinterpret_cast<const half2*>(&wv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fw = __half22float2(pw[e]), fx = __half22float2(px[e]);
+            acc[r] = fmaf(fw.x, fx.x, acc[r]);
+            acc[r] = fmaf(fw.y, fx.y, acc[r]);
+          }
+        }
       }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) p.h_res[r0 + r] = __float2half(hres + round_half(acc + bias));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < kResidRows; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kResidRows; ++r) red[warp][r] = acc[r];
+  }
+  __syncthreads();
+  if (owner) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kResidThreads / 32; ++w) sum += red[w][tid];
+    p.h_res[r0 + tid] = __float2half(hres + round_half(sum + bias));
   }
 }
 
@@ -1141,10 +1263,10 @@ static int rows_for(int n_out) {
   return kSmallRows;
 }
 
-template <int kAct>
-static int launch_ln_gemv(const GemvParams& p, cudaStream_t s, bool pdl) {
+template <int kAct, int kRowsPerWarp>
+static int launch_ln_gemv_t(const GemvParams& p, cudaStream_t s, bool pdl) {
   const int smem = p.rows_per_cta * kHidden * 2;
-  auto kern = ln_gemv_kernel<kAct>;
+  auto kern = ln_gemv_kernel<kAct, kRowsPerWarp>;
   cudaError_t e = ensure_smem(kern, smem);
   if (e == cudaSuccess) {
     const int grid = (p.n_out + p.rows_per_cta - 1) / p.rows_per_cta;
@@ -1153,15 +1275,32 @@ static int launch_ln_gemv(const GemvParams& p, cudaStream_t s, bool pdl) {
   return launch_status(e, "ln_gemv");
 }
 
-static int launch_gemv_residual(const GemvParams& p, cudaStream_t s, bool pdl) {
-  if (p.rows_per_cta != kSmallRows) return set_error(FW_ERR_ARG, "gemv_residual: rows_per_cta must be %d", kSmallRows);
-  const int smem = (p.rows_per_cta + 1) * p.k * 2;
-  cudaError_t e = ensure_smem(gemv_residual_kernel, smem);
+template <int kAct>
+static int launch_ln_gemv(const GemvParams& p, cudaStream_t s, bool pdl) {
+  switch (p.rows_per_cta) {
+    case 8: return launch_ln_gemv_t<kAct, 1>(p, s, pdl);
+    case 24: return launch_ln_gemv_t<kAct, 3>(p, s, pdl);
+    case 32: return launch_ln_gemv_t<kAct, 4>(p, s, pdl);
+    default: return set_error(FW_ERR_ARG, "ln_gemv: rows_per_cta must be 8, 24 or 32");
+  }
+}
+
+template <int kChunks>
+static int launch_gemv_residual_t(const GemvParams& p, cudaStream_t s, bool pdl) {
+  auto kern = gemv_residual_kernel<kChunks>;
+  const int smem = kResidRows * 256 * kChunks * 2;
+  cudaError_t e = ensure_smem(kern, smem);
   if (e == cudaSuccess) {
-    const int grid = (p.n_out + p.rows_per_cta - 1) / p.rows_per_cta;
-    e = launch(gemv_residual_kernel, dim3(grid), dim3(256), smem, s, pdl, p);
+    const int grid = (p.n_out + kResidRows - 1) / kResidRows;
+    e = launch(kern, dim3(grid), dim3(kResidThreads), smem, s, pdl, p);
   }
   return launch_status(e, "gemv_residual");
+}
+
+static int launch_gemv_residual(const GemvParams& p, cudaStream_t s, bool pdl) {
+  if (p.k == kHidden) return launch_gemv_residual_t<kHidden / 256>(p, s, pdl);
+  if (p.k == kFfn) return launch_gemv_residual_t<kFfn / 256>(p, s, pdl);
+  return set_error(FW_ERR_SHAPE, "gemv_residual: k must be %d or %d", kHidden, kFfn);
 }
 
 static int launch_attention(const AttnParams& p, int heads, int splits, cudaStream_t s, bool pdl) {
@@ -1185,6 +1324,8 @@ static int launch_lm_head(LmParams p, cudaStream_t s, bool pdl) {
   if (e == cudaSuccess) {
     const int grid = num_sms();
     p.rows_per_cta = (p.vocab + grid - 1) / grid;
+    if (p.rows_per_cta > kLmMaxRowsPerCta)
+      return set_error(FW_ERR_SHAPE, "lm_head_argmax: vocab must be <= %d", kLmMaxRowsPerCta * grid);
     e = launch(kern, dim3(grid), dim3(256), kLmSmem, s, pdl, p);
   }
   return launch_status(e, "lm_head_argmax");
@@ -1402,7 +1543,7 @@ int fw_ln_gemv(const void* h, const void* gamma, const void* beta, float eps, co
 
 int fw_gemv_residual(const void* x, int k, const void* w, const void* b, void* h, int n_out, fw_stream_t stream) {
   FW_REQUIRE(x && w && h, FW_ERR_NULL, "gemv_residual: x, w and h are required");
-  FW_REQUIRE(k > 0 && k % 256 == 0 && k <= 8192, FW_ERR_SHAPE, "gemv_residual: k must be a multiple of 256, <= 8192");
+  FW_REQUIRE(k == kHidden || k == kFfn, FW_ERR_SHAPE, "gemv_residual: k must be %d or %d", kHidden, kFfn);
   FW_REQUIRE(n_out > 0, FW_ERR_SHAPE, "gemv_residual: n_out must be positive");
   FW_REQUIRE(aligned16(w) && aligned16(x), FW_ERR_ALIGN, "gemv_residual: w and x must be 16-byte aligned");
   GemvParams p{};
@@ -1410,7 +1551,7 @@ int fw_gemv_residual(const void* x, int k, const void* w, const void* b, void* h
   p.b = static_cast<const half*>(b);
   p.n_out = n_out;
   p.k = k;
-  p.rows_per_cta = kSmallRows;
+  p.rows_per_cta = kResidRows;
   p.x = static_cast<const half*>(x);
   p.h_res = static_cast<half*>(h);
   return launch_gemv_residual(p, static_cast<cudaStream_t>(stream), false);
@@ -1507,7 +1648,7 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
       r.b = static_cast<const half*>(L.fc2_b);
       r.n_out = kHidden;
       r.k = kFfn;
-      r.rows_per_cta = kSmallRows;
+      r.rows_per_cta = kResidRows;
       r.x = ffn;
       r.h_res = h;
       if ((rc = launch_gemv_residual(r, s, true))) return rc;

@@ -123,7 +123,7 @@ int fw_argmax_f16(const void* logits, int64_t n, const bool* suppress, int64_t* 
 int fw_ln_gemv(const void* h, const void* gamma, const void* beta, float eps, const void* w, const void* b,
                void* out, int n_out, int hidden, int act, fw_stream_t stream);
 
-/* h[r] = fp16(h[r] + fp16(W[r] . x + b[r])) for r < n_out; x has k elements (k % 256 == 0).
+/* h[r] = fp16(h[r] + fp16(W[r] . x + b[r])) for r < n_out; x has k elements (k = 1280 or 5120).
  * Fuses F.linear (custom/model.py:116,119,120) with the residual add of the next add_layernorm. */
 int fw_gemv_residual(const void* x, int k, const void* w, const void* b, void* h, int n_out, fw_stream_t stream);
 
