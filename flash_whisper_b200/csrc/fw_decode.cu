@@ -643,7 +643,6 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   __syncthreads();
   cluster_arrive_relaxed();  // completed by the wait before the first DSMEM store: all CTAs are running
   pdl_wait();
-  pdl_trigger();
 
   // ---- 1. LayerNorm prologue and this CTA's projection rows ----
   if (kEmbed || (kSelf && !p.state_early)) {
@@ -691,6 +690,10 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     }
   }
   cluster.sync();  // q (| k | v) of this head visible in every CTA
+  // The next launch is released only now: its weight prefetch (a burst of bulk copies) would
+  // otherwise queue in front of this kernel's loads of h, and this kernel runs long enough after
+  // this point for that prefetch to complete.
+  pdl_trigger();
   if (tid == 0) {  // every thread of this CTA is past its reads of the projection rows
     fence_proxy_async_shared();
     mbar_arrive_expect_tx(&bar_o, S::kOutBytes);
