@@ -176,39 +176,75 @@ __device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int
   reinterpret_cast<uint4*>(dst)[1] = w1;
 }
 
-template <int BN, int STAGES, bool kConv>
+// Persistent warp-specialised GEMM. CTA b processes output tiles b, b + gridDim.x, ... in n-major
+// order (tile t covers m tile t % m_tiles and n tile t / m_tiles), so the CTAs that run together
+// share weight (B) slices. Warp 0 streams A and B k-blocks through a STAGES-deep ring (the B
+// tiles of the first stages are requested before the PDL wait), warp 1 issues the MMAs into one of
+// kAccBufs TMEM accumulators, warps 2-5 drain the previous accumulator through the epilogue while
+// the next tile's MMAs run. BN = kSub * kSubN columns per tile: kSub MMAs of N = kSubN per K step.
+template <int kSubN, int kSub, int STAGES, bool kConv>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB, int num_kb,
-                                                         int conv_c, int conv_stride, GemmEpi ep) {
+                                                         int conv_c, int conv_stride, GemmEpi ep, int m_tiles,
+                                                         int n_tiles, const char* l2_next, unsigned l2_bytes) {
   constexpr int BM = 128, BK = 64;
+  constexpr int BN = kSubN * kSub;
   constexpr uint32_t kABytes = BM * BK * 2;
+  constexpr uint32_t kBSubBytes = kSubN * BK * 2;
   constexpr uint32_t kBBytes = BN * BK * 2;
   constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  constexpr int kAccBufs = 2 * BN <= 512 ? 2 : 1;
+  constexpr uint32_t kTmemCols = BN * kAccBufs <= 64 ? 64 : BN * kAccBufs <= 128 ? 128 : BN * kAccBufs <= 256 ? 256 : 512;
+  static_assert(BN * kAccBufs <= 512, "accumulators exceed TMEM");
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t tmem_bar;
+  __shared__ __align__(8) uint64_t acc_full[kAccBufs];
+  __shared__ __align__(8) uint64_t acc_empty[kAccBufs];
   __shared__ uint32_t tmem_base_sh;
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM;
-  const int n0 = blockIdx.y * BN;
+  const int tiles = m_tiles * n_tiles;
+  const int first = blockIdx.x;
+  const int pre = num_kb < STAGES ? num_kb : STAGES;
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&tmem_bar, 1);
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (first < tiles) {  // weight tiles of the first stages do not depend on the previous kernel
+      const int n0 = (first / m_tiles) * BN;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full_bar[kb], kStageBytes);
+#pragma unroll
+        for (int j = 0; j < kSub; ++j)
+          tma_load_2d(smem + kb * kStageBytes + kABytes + j * kBSubBytes, &tmB, &full_bar[kb], kb * BK,
+                      n0 + j * kSubN);
+      }
+    }
+    // warm L2 with this CTA's share of the weights of the next GEMM
+    if (l2_next != nullptr && l2_bytes > 0) {
+      const unsigned share = ((l2_bytes + gridDim.x - 1) / gridDim.x + 15u) & ~15u;
+      const unsigned off = share * blockIdx.x;
+      if (off < l2_bytes) {
+        const unsigned n = min(share, l2_bytes - off);
+        for (unsigned o = 0; o < n; o += 65536u) l2_prefetch(l2_next + off + o, min(65536u, n - o));
+      }
+    }
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_sh, BN);
+    tmem_alloc(&tmem_base_sh, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -218,75 +254,108 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 
   if (warp == 0) {
     if (lane == 0) {
-      const int pre = num_kb < STAGES ? num_kb : STAGES;
-      for (int kb = 0; kb < pre; ++kb) {  // weight tiles do not depend on the previous kernel
-        mbar_arrive_expect_tx(&full_bar[kb], kStageBytes);
-        tma_load_2d(smem + kb * kStageBytes + kABytes, &tmB, &full_bar[kb], kb * BK, n0);
-      }
       pdl_wait();
       pdl_trigger();
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1u;
-        uint8_t* sa = smem + s * kStageBytes;
-        if (kb >= STAGES) {
-          if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
-            enc_flag(FW_DEVERR_TIMEOUT);
-            break;
+      int it = 0;  // k-block counter across tiles (ring position)
+      for (int t = first; t < tiles; t += gridDim.x) {
+        const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          uint8_t* sa = smem + s * kStageBytes;
+          const bool b_loaded = t == first && kb < pre;
+          if (!b_loaded) {
+            if (it >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u)) {
+              enc_flag(FW_DEVERR_TIMEOUT);
+              t = tiles;
+              break;
+            }
+            mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+#pragma unroll
+            for (int j = 0; j < kSub; ++j)
+              tma_load_2d(sa + kABytes + j * kBSubBytes, &tmB, &full_bar[s], kb * BK, n0 + j * kSubN);
           }
-          mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
-          tma_load_2d(sa + kABytes, &tmB, &full_bar[s], kb * BK, n0);
-        }
-        if (kConv) {
-          const int k = kb * BK;
-          const int tap = k / conv_c;
-          const int c0 = k - tap * conv_c;
-          tma_load_3d(sa, &tmA, &full_bar[s], c0, tap % conv_stride, m0 + tap / conv_stride);
-        } else {
-          tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, m0);
+          if (kConv) {
+            const int k = kb * BK;
+            const int tap = k / conv_c;
+            const int c0 = k - tap * conv_c;
+            tma_load_3d(sa, &tmA, &full_bar[s], c0, tap % conv_stride, m0 + tap / conv_stride);
+          } else {
+            tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, m0);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(BM, BN);
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1u;
-        if (!mbar_wait(&full_bar[s], ph)) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, kSubN);
+      int it = 0, local = 0;
+      for (int t = first; t < tiles; t += gridDim.x, ++local) {
+        const int buf = local % kAccBufs;
+        const uint32_t use = local / kAccBufs;
+        if (local >= kAccBufs && !mbar_wait(&acc_empty[buf], (use - 1) & 1u)) {  // epilogue drained it
           enc_flag(FW_DEVERR_TIMEOUT);
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = base + s * kStageBytes;
-        const uint64_t adesc = sw128_desc(a_addr);
-        const uint64_t bdesc = sw128_desc(a_addr + kABytes);
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&full_bar[s], ph)) {
+            enc_flag(FW_DEVERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = base + s * kStageBytes;
+          const uint64_t adesc = sw128_desc(a_addr);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          tc_mma_f16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
-        tc_commit(&empty_bar[s]);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+#pragma unroll
+            for (int j = 0; j < kSub; ++j)
+              tc_mma_f16(d + j * kSubN, adesc + 2 * kk, sw128_desc(a_addr + kABytes + j * kBSubBytes) + 2 * kk, idesc,
+                         (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[s]);
+        }
+        tc_commit(&acc_full[buf]);
+        if (!ok) break;
       }
-      tc_commit(&tmem_bar);
     }
   } else {
     pdl_wait();
     const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to this warp
-    const int row = m0 + q * 32 + lane;
-    if (!mbar_wait(&tmem_bar, 0)) enc_flag(FW_DEVERR_TIMEOUT);
-    tc_fence_after();
+    int local = 0;
+    for (int t = first; t < tiles; t += gridDim.x, ++local) {
+      const int buf = local % kAccBufs;
+      const uint32_t use = local / kAccBufs;
+      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      const int row = m0 + q * 32 + lane;
+      if (!mbar_wait(&acc_full[buf], use & 1u)) {
+        enc_flag(FW_DEVERR_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t r[16];
-      tc_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), r);
-      tc_wait_ld();
-      if (row < ep.M) epilogue_store16(ep, row, n0 + c, r);
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tc_ld16(d + static_cast<uint32_t>(c), r);
+        tc_wait_ld();
+        if (row < ep.M) epilogue_store16(ep, row, n0 + c, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -586,41 +655,69 @@ static int make_map_conv(CUtensorMap* m, const void* ptr, int C, int rows, int s
   return FW_OK;
 }
 
-template <int BN, int STAGES, bool kConv>
+template <int kSubN, int kSub, int STAGES, bool kConv>
 static int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int K, int conv_c, int conv_stride,
-                         const GemmEpi& ep, cudaStream_t s, bool pdl) {
+                         const GemmEpi& ep, const void* l2_next, size_t l2_bytes, cudaStream_t s, bool pdl) {
+  constexpr int BN = kSubN * kSub;
   constexpr int smem = STAGES * (128 * 64 * 2 + BN * 64 * 2) + 1024;
-  auto kern = gemm_tc_kernel<BN, STAGES, kConv>;
+  auto kern = gemm_tc_kernel<kSubN, kSub, STAGES, kConv>;
   cudaError_t e = ensure_smem(kern, smem);
   if (e == cudaSuccess) {
-    dim3 grid((ep.M + 127) / 128, ep.N / BN);
-    e = launch(kern, grid, dim3(192), smem, s, pdl, ta, tb, K / 64, conv_c, conv_stride, ep);
+    const int m_tiles = (ep.M + 127) / 128, n_tiles = ep.N / BN;
+    const int tiles = m_tiles * n_tiles;
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    e = launch(kern, dim3(grid), dim3(192), smem, s, pdl, ta, tb, K / 64, conv_c, conv_stride, ep, m_tiles, n_tiles,
+               static_cast<const char*>(l2_next), static_cast<unsigned>(l2_bytes));
   }
   return launch_status(e, "gemm_tc");
 }
 
-// Picks the N tile so that the grid covers the 148 SMs reasonably (M is 1500 or 3000 here).
+// Picks the N tile: the fewest tile rounds per SM, weighted by the tile width (a round costs time
+// proportional to BN) and by the lower tensor efficiency of narrow tiles. The 320-wide tile has a
+// single TMEM accumulator (its epilogue cannot overlap a next tile), so it is used only when every
+// CTA gets exactly one tile.
 static int pick_bn(int M, int N) {
-  const int mt = (M + 127) / 128;
-  if (N % 256 == 0 && mt * (N / 256) >= 148) return 256;
-  if (N % 128 == 0 && mt * (N / 128) >= 148) return 128;
-  return 64;
+  const int mt = (M + 127) / 128, sms = num_sms();
+  static const int kBn[4] = {320, 256, 128, 64};
+  static const float kEff[4] = {1.0f, 1.0f, 0.85f, 0.7f};
+  int best = 64;
+  float best_cost = 1e30f;
+  for (int i = 0; i < 4; ++i) {
+    if (N % kBn[i]) continue;
+    const int tiles = mt * (N / kBn[i]);
+    const int rounds = (tiles + sms - 1) / sms;
+    if (kBn[i] == 320 && rounds > 1) continue;
+    const float cost = rounds * kBn[i] / kEff[i];
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = kBn[i];
+    }
+  }
+  return best;
 }
 
 static int gemm_dispatch(const CUtensorMap& ta, const void* B, int64_t ldb, int K, int conv_c, int conv_stride,
-                         bool conv, const GemmEpi& ep, cudaStream_t s, bool pdl) {
+                         bool conv, const GemmEpi& ep, const void* l2_next, size_t l2_bytes, cudaStream_t s,
+                         bool pdl) {
   const int bn = pick_bn(ep.M, ep.N);
   CUtensorMap tb;
-  int rc = make_map_2d(&tb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(ep.N), static_cast<uint64_t>(ldb), bn);
+  int rc = make_map_2d(&tb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(ep.N), static_cast<uint64_t>(ldb),
+                       bn == 320 ? 160 : bn);
   if (rc) return rc;
   if (conv) {
-    if (bn == 256) return launch_gemm_t<256, 4, true>(ta, tb, K, conv_c, conv_stride, ep, s, pdl);
-    if (bn == 128) return launch_gemm_t<128, 3, true>(ta, tb, K, conv_c, conv_stride, ep, s, pdl);
-    return launch_gemm_t<64, 4, true>(ta, tb, K, conv_c, conv_stride, ep, s, pdl);
+    switch (bn) {
+      case 320: return launch_gemm_t<160, 2, 4, true>(ta, tb, K, conv_c, conv_stride, ep, l2_next, l2_bytes, s, pdl);
+      case 256: return launch_gemm_t<256, 1, 4, true>(ta, tb, K, conv_c, conv_stride, ep, l2_next, l2_bytes, s, pdl);
+      case 128: return launch_gemm_t<128, 1, 6, true>(ta, tb, K, conv_c, conv_stride, ep, l2_next, l2_bytes, s, pdl);
+      default: return launch_gemm_t<64, 1, 8, true>(ta, tb, K, conv_c, conv_stride, ep, l2_next, l2_bytes, s, pdl);
+    }
   }
-  if (bn == 256) return launch_gemm_t<256, 4, false>(ta, tb, K, 0, 1, ep, s, pdl);
-  if (bn == 128) return launch_gemm_t<128, 3, false>(ta, tb, K, 0, 1, ep, s, pdl);
-  return launch_gemm_t<64, 4, false>(ta, tb, K, 0, 1, ep, s, pdl);
+  switch (bn) {
+    case 320: return launch_gemm_t<160, 2, 4, false>(ta, tb, K, 0, 1, ep, l2_next, l2_bytes, s, pdl);
+    case 256: return launch_gemm_t<256, 1, 4, false>(ta, tb, K, 0, 1, ep, l2_next, l2_bytes, s, pdl);
+    case 128: return launch_gemm_t<128, 1, 6, false>(ta, tb, K, 0, 1, ep, l2_next, l2_bytes, s, pdl);
+    default: return launch_gemm_t<64, 1, 8, false>(ta, tb, K, 0, 1, ep, l2_next, l2_bytes, s, pdl);
+  }
 }
 
 static int check_epi(const GemmEpi& ep, int K) {
@@ -639,7 +736,7 @@ static int check_epi(const GemmEpi& ep, int K) {
 }
 
 static int run_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int K, const GemmEpi& ep, cudaStream_t s,
-                    bool pdl) {
+                    bool pdl, const void* l2_next = nullptr, size_t l2_bytes = 0) {
   int rc = check_epi(ep, K);
   if (rc) return rc;
   FW_REQUIRE(A && B, FW_ERR_NULL, "gemm: A and B are required");
@@ -648,11 +745,11 @@ static int run_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, int 
   CUtensorMap ta;
   rc = make_map_2d(&ta, A, static_cast<uint64_t>(K), static_cast<uint64_t>(ep.M), static_cast<uint64_t>(lda), 128);
   if (rc) return rc;
-  return gemm_dispatch(ta, B, ldb, K, 0, 1, false, ep, s, pdl);
+  return gemm_dispatch(ta, B, ldb, K, 0, 1, false, ep, l2_next, l2_bytes, s, pdl);
 }
 
 static int run_conv(const void* X, int C, int rows_padded, int stride, const void* W, const GemmEpi& ep,
-                    cudaStream_t s, bool pdl) {
+                    cudaStream_t s, bool pdl, const void* l2_next = nullptr, size_t l2_bytes = 0) {
   const int K = 3 * C;
   int rc = check_epi(ep, K);
   if (rc) return rc;
@@ -664,7 +761,7 @@ static int run_conv(const void* X, int C, int rows_padded, int stride, const voi
   CUtensorMap ta;
   rc = make_map_conv(&ta, X, C, rows_padded, stride);
   if (rc) return rc;
-  return gemm_dispatch(ta, W, K, K, C, stride, true, ep, s, pdl);
+  return gemm_dispatch(ta, W, K, K, C, stride, true, ep, l2_next, l2_bytes, s, pdl);
 }
 
 static int run_layernorm(const void* x, const void* g, const void* b, void* y, int rows, int cols, float eps,
@@ -751,21 +848,27 @@ int fw_encoder_forward(const fw_encoder_t* e, fw_stream_t stream) {
   // conv2 (stride 2) + GELU + sinusoid positions -> x
   ep = GemmEpi{static_cast<const half*>(e->conv2_b), x, kHidden, static_cast<const half*>(e->pos), kHidden, T, kHidden,
                FW_EPI_GELU_POS, 1.f, 0};
-  if ((rc = run_conv(conv1_out, kHidden, F + 2, 2, e->conv2_w, ep, s, true))) return rc;
+  // Each GEMM warms L2 with the weights of the next GEMM in the layer sequence (qkv -> out -> fc1 ->
+  // fc2 -> next layer's qkv), so their tile loads hit L2 instead of waiting on HBM.
+  const size_t kSq = size_t(kHidden) * kHidden * 2, kFf = size_t(kFfn) * kHidden * 2;
+  if ((rc = run_conv(conv1_out, kHidden, F + 2, 2, e->conv2_w, ep, s, true,
+                     e->n_layers > 0 ? e->layers[0].qkv_w : nullptr, 3 * kSq)))
+    return rc;
   for (int l = 0; l < e->n_layers; ++l) {
     const fw_encoder_layer_t& L = e->layers[l];
+    const void* next_qkv = l + 1 < e->n_layers ? e->layers[l + 1].qkv_w : nullptr;
     if ((rc = run_layernorm(x, L.ln1_g, L.ln1_b, y, T, kHidden, e->eps, s, true))) return rc;
     ep = GemmEpi{static_cast<const half*>(L.qkv_b), qkv, 3 * kHidden, nullptr, 0, T, 3 * kHidden,
                  FW_EPI_BIAS_SCALE, 0.125f, kHidden};
-    if ((rc = run_gemm(y, kHidden, L.qkv_w, kHidden, kHidden, ep, s, true))) return rc;
+    if ((rc = run_gemm(y, kHidden, L.qkv_w, kHidden, kHidden, ep, s, true, L.out_w, kSq))) return rc;
     if ((rc = run_attention(qkv, 3 * kHidden, kHidden, 2 * kHidden, attn, T, e->heads, s, true))) return rc;
     ep = GemmEpi{static_cast<const half*>(L.out_b), x, kHidden, x, kHidden, T, kHidden, FW_EPI_BIAS_RESID, 1.f, 0};
-    if ((rc = run_gemm(attn, kHidden, L.out_w, kHidden, kHidden, ep, s, true))) return rc;
+    if ((rc = run_gemm(attn, kHidden, L.out_w, kHidden, kHidden, ep, s, true, L.fc1_w, kFf))) return rc;
     if ((rc = run_layernorm(x, L.ln2_g, L.ln2_b, y, T, kHidden, e->eps, s, true))) return rc;
     ep = GemmEpi{static_cast<const half*>(L.fc1_b), ffn, kFfn, nullptr, 0, T, kFfn, FW_EPI_BIAS_GELU, 1.f, 0};
-    if ((rc = run_gemm(y, kHidden, L.fc1_w, kHidden, kHidden, ep, s, true))) return rc;
+    if ((rc = run_gemm(y, kHidden, L.fc1_w, kHidden, kHidden, ep, s, true, L.fc2_w, kFf))) return rc;
     ep = GemmEpi{static_cast<const half*>(L.fc2_b), x, kHidden, x, kHidden, T, kHidden, FW_EPI_BIAS_RESID, 1.f, 0};
-    if ((rc = run_gemm(ffn, kFfn, L.fc2_w, kFfn, kFfn, ep, s, true))) return rc;
+    if ((rc = run_gemm(ffn, kFfn, L.fc2_w, kFfn, kFfn, ep, s, true, next_qkv, 3 * kSq))) return rc;
   }
   if ((rc = run_layernorm(x, e->final_g, e->final_b, e->enc_out, T, kHidden, e->eps, s, true))) return rc;
   const int ncross = e->n_dec_layers * 2 * kHidden;
