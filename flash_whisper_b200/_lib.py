@@ -15,7 +15,7 @@ LIB_PATH = PKG / 'libflashwhisper.so'
 HEADER = PKG.parent / 'include' / 'flash_whisper.h'
 
 FW_OK = 0
-FW_EPI_BIAS, FW_EPI_BIAS_GELU, FW_EPI_BIAS_RESID, FW_EPI_GELU_POS, FW_EPI_CROSS_KV, FW_EPI_BIAS_SCALE = range(6)
+FW_EPI_BIAS, FW_EPI_BIAS_GELU, FW_EPI_BIAS_RESID, FW_EPI_GELU_POS, FW_EPI_CROSS_KV, FW_EPI_BIAS_SCALE, FW_EPI_QKV_VT = range(7)
 MAX_LAYERS = 8
 MAX_ENC_LAYERS = 32
 
@@ -56,6 +56,7 @@ class Encoder(ctypes.Structure):
         ('final_g', vp), ('final_b', vp), ('cross_w', vp), ('cross_b', vp),
         ('conv1_out', vp), ('x', vp), ('y', vp), ('qkv', vp), ('attn', vp), ('ffn', vp), ('enc_out', vp),
         ('cross_kv', vp),
+        ('vt', vp),
     ]
 
 
@@ -81,7 +82,7 @@ _SIGNATURES = {
     'fw_conv1d_k3_f16': (c_int, [vp, c_int, c_int, c_int, vp, vp, vp, c_int64, vp, c_int64, c_int, c_int, c_int,
                                  vp]),
     'fw_layernorm_rows': (c_int, [vp, vp, vp, vp, c_int, c_int, c_float, vp]),
-    'fw_encoder_attention': (c_int, [vp, c_int64, c_int, c_int, vp, c_int, c_int, vp]),
+    'fw_encoder_attention': (c_int, [vp, c_int64, c_int, c_int, vp, c_int, c_int, vp, vp]),
     'fw_encoder_forward': (c_int, [POINTER(Encoder), vp]),
 }
 

@@ -66,6 +66,12 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// tcgen05.ld / st / wait are .sync.aligned: every lane of the warp must execute them together, so
+// any condition in front of them must be warp-uniform. This wait returns the same result in all lanes.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, unsigned parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -118,6 +124,7 @@ struct GemmEpi {
   int mode;
   float scale;
   int scale_cols;
+  int vt_col;  // FW_EPI_QKV_VT: first column written transposed into R
 };
 
 __device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int n, const uint32_t (&r)[16]) {
@@ -140,6 +147,12 @@ __device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int
 #pragma unroll
   for (int j = 0; j < 16; ++j) o[j] = round_half(__uint_as_float(r[j]) + bias[j]);
 
+  if (ep.mode == FW_EPI_QKV_VT && n >= ep.vt_col) {  // V: transposed store, R[(n - vt_col) * ldr + row]
+    half* vt = const_cast<half*>(ep.R) + static_cast<size_t>(n - ep.vt_col) * ep.ldr + row;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) vt[static_cast<size_t>(j) * ep.ldr] = __float2half(o[j]);
+    return;
+  }
   half* dst;
   if (ep.mode == FW_EPI_CROSS_KV) {
     dst = ep.C + (static_cast<size_t>(n >> 6) * ep.M + row) * 64 + (n & 63);
@@ -159,7 +172,7 @@ __device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int
       const float res = __half2float(j < 8 ? rh0[j] : rh1[j - 8]);
       o[j] = ep.mode == FW_EPI_GELU_POS ? round_half(gelu_erf(o[j])) + res : res + o[j];
     }
-  } else if (ep.mode == FW_EPI_BIAS_SCALE) {
+  } else if (ep.mode == FW_EPI_BIAS_SCALE || ep.mode == FW_EPI_QKV_VT) {
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (n + j < ep.scale_cols) o[j] = o[j] * ep.scale;
@@ -333,7 +346,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       const uint32_t use = local / kAccBufs;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
       const int row = m0 + q * 32 + lane;
-      if (!mbar_wait(&acc_full[buf], use & 1u)) {
+      if (!mbar_wait_warp(&acc_full[buf], use & 1u)) {
         enc_flag(FW_DEVERR_TIMEOUT);
         break;
       }
@@ -418,189 +431,273 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const half* __restr
 }
 
 // ------------------------------------------------------------------------------------------------
-// Encoder attention (mma.sync m16n8k16, fp16 in, fp32 accumulate/softmax).
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+// Encoder attention on tcgen05 (bidirectional, one head, kAttnQ queries per CTA, 64-key blocks).
+//   warp 0 (one lane): TMA loads - Q once, then K and V^T blocks through a kAttnStages ring
+//   warp 1 (one lane): S = Q K^T into TMEM, then O += P V into TMEM, one 64-key block at a time;
+//                      S of block j + 1 is issued as soon as the softmax has read S of block j
+//   warps 2-5: one thread per query row (TMEM lane): online softmax of S (exp2, running max and
+//              sum in fp32), P as fp16 into a 128B-swizzled K-major shared tile (the A operand of
+//              the P V MMA), rescaling of the O row in TMEM when the running max grows, and the
+//              final O / l store.
+// V is read transposed ([heads * 64, seq_pad], keys contiguous) so both MMAs use K-major operands.
+// q arrives pre-scaled by 1/8 (HF WhisperAttention), so S is used unscaled.
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
 }
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
-// Byte offset of 16-byte chunk `c` of row `r` in a [rows x 64] fp16 tile with XOR swizzle.
-__device__ __forceinline__ uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-constexpr int kEncQ = 128;
-constexpr int kEncK = 64;
+constexpr int kAttnQ = 128;
+constexpr int kAttnK = 64;
+constexpr int kAttnStages = 3;
+constexpr uint32_t kAttnQBytes = kAttnQ * 64 * 2;   // 16 KB
+constexpr uint32_t kAttnKBytes = kAttnK * 64 * 2;   // 8 KB
+constexpr uint32_t kAttnPBytes = kAttnQ * kAttnK * 2;  // 16 KB
+constexpr int kAttnSmem = kAttnQBytes + 2 * kAttnStages * kAttnKBytes + kAttnPBytes + 1024;
 
-__global__ void __launch_bounds__(256) enc_attention_kernel(const half* __restrict__ qkv, int64_t ld, int kcol,
-                                                            int vcol, half* __restrict__ out, int seq) {
-  __shared__ __align__(128) uint8_t qs[kEncQ * 128];
-  __shared__ __align__(128) uint8_t ks[2][kEncK * 128];
-  __shared__ __align__(128) uint8_t vs[2][kEncK * 128];
-  const int head = blockIdx.y;
-  const int q0 = blockIdx.x * kEncQ;
+__global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQK,
+                                                             const __grid_constant__ CUtensorMap tmVt, int kcol,
+                                                             half* __restrict__ out, int ldo, int seq) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_q, full_k[kAttnStages], empty_k[kAttnStages], full_v[kAttnStages],
+      empty_v[kAttnStages], s_full, s_free, p_full, o_done;
+  __shared__ uint32_t tmem_base_sh;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  uint8_t* qs = smem;
+  uint8_t* ks = smem + kAttnQBytes;
+  uint8_t* vts = ks + kAttnStages * kAttnKBytes;
+  uint8_t* ps = vts + kAttnStages * kAttnKBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
+  const int head = blockIdx.y;
+  const int q0 = blockIdx.x * kAttnQ;
+  const int nkb = (seq + kAttnK - 1) / kAttnK;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(&bar_q, 1);
+    for (int i = 0; i < kAttnStages; ++i) {
+      mbar_init(&full_k[i], 1);
+      mbar_init(&empty_k[i], 1);
+      mbar_init(&full_v[i], 1);
+      mbar_init(&empty_v[i], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&s_free, 4);
+    mbar_init(&p_full, 4);
+    mbar_init(&o_done, 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmQK);
+    tma_prefetch_desc(&tmVt);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, 128);  // S: columns 0-63, O: columns 64-127
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
   pdl_wait();
   pdl_trigger();
 
-  auto load_kv = [&](int kb, int buf) {
-    for (int i = threadIdx.x; i < kEncK * 8; i += 256) {
-      const int r = i >> 3, c = i & 7;
-      const int key = kb * kEncK + r;
-      const bool ok = key < seq;
-      const size_t rowoff = static_cast<size_t>(ok ? key : 0) * ld;
-      cp_async16(ks[buf] + swz(r, c), qkv + rowoff + kcol + head * 64 + c * 8, ok);
-      cp_async16(vs[buf] + swz(r, c), qkv + rowoff + vcol + head * 64 + c * 8, ok);
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar_q, kAttnQBytes);
+      tma_load_2d(qs, &tmQK, &bar_q, head * 64, q0);  // the map's box is 64 rows: Q is two boxes
+      tma_load_2d(qs + kAttnKBytes, &tmQK, &bar_q, head * 64, q0 + 64);
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % kAttnStages;
+        const uint32_t ph = (j / kAttnStages) & 1u;
+        if (j >= kAttnStages && !mbar_wait(&empty_k[st], ph ^ 1u)) {
+          enc_flag(FW_DEVERR_TIMEOUT);
+          break;
+        }
+        mbar_arrive_expect_tx(&full_k[st], kAttnKBytes);
+        tma_load_2d(ks + st * kAttnKBytes, &tmQK, &full_k[st], kcol + head * 64, j * kAttnK);
+        if (j >= kAttnStages && !mbar_wait(&empty_v[st], ph ^ 1u)) {
+          enc_flag(FW_DEVERR_TIMEOUT);
+          break;
+        }
+        mbar_arrive_expect_tx(&full_v[st], kAttnKBytes);
+        tma_load_2d(vts + st * kAttnKBytes, &tmVt, &full_v[st], j * kAttnK, head * 64);
+      }
     }
-  };
-  for (int i = threadIdx.x; i < kEncQ * 8; i += 256) {
-    const int r = i >> 3, c = i & 7;
-    const int qi = q0 + r;
-    const bool ok = qi < seq;
-    cp_async16(qs + swz(r, c), qkv + static_cast<size_t>(ok ? qi : 0) * ld + head * 64 + c * 8, ok);
-  }
-  load_kv(0, 0);
-  cp_async_commit();
-
-  const int nkb = (seq + kEncK - 1) / kEncK;
-  uint32_t qa[4][4];
-  float o[8][4];
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(kAttnQ, 64);  // S: N = 64 keys; O: N = 64 dims
+      const uint32_t s_tmem = tmem, o_tmem = tmem + 64;
+      bool ok = mbar_wait(&bar_q, 0);
+      auto issue_s = [&](int j) {  // S = Q K_j^T
+        const int st = j % kAttnStages;
+        if (!mbar_wait(&full_k[st], (j / kAttnStages) & 1u)) return false;
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(base), bd = sw128_desc(smem_u32(ks + st * kAttnKBytes));
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float mrow[2] = {-INFINITY, -INFINITY};
-  float lrow[2] = {0.f, 0.f};
-  constexpr float kLog2e = 1.4426950408889634f;
-  const uint32_t qs_base = smem_u32(qs);
-
-  for (int kb = 0; kb < nkb; ++kb) {
-    const int buf = kb & 1;
-    if (kb + 1 < nkb) {
-      load_kv(kb + 1, buf ^ 1);
-      cp_async_commit();
-      cp_async_wait<1>();
+        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(s_tmem, ad + 2 * kk, bd + 2 * kk, idesc, kk != 0 ? 1u : 0u);
+        tc_commit(&empty_k[st]);
+        tc_commit(&s_full);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < nkb; ++j) {
+        // S_{j+1} may overwrite S as soon as the softmax has read S_j
+        if (!mbar_wait(&s_free, j & 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (j + 1 < nkb && !(ok = issue_s(j + 1))) break;
+        // O += P_j V_j
+        const int st = j % kAttnStages;
+        if (!mbar_wait(&p_full, j & 1u) || !mbar_wait(&full_v[st], (j / kAttnStages) & 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(smem_u32(ps)), bd = sw128_desc(smem_u32(vts + st * kAttnKBytes));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_f16(o_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (j | kk) != 0 ? 1u : 0u);
+        tc_commit(&empty_v[st]);
+        tc_commit(&o_done);
+      }
+      if (!ok) enc_flag(FW_DEVERR_TIMEOUT);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lanes 32q..32q+31
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    constexpr float kLog2e = 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      if (!mbar_wait_warp(&s_full, j & 1u)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[16];
+        tc_ld16(lane_base + c * 16, u);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sv[c * 16 + i] = __uint_as_float(u[i]) * kLog2e;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free);  // S may now be overwritten by the next block's MMA
+      const int kvalid = seq - j * kAttnK;
+      float mb = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        if (i >= kvalid) sv[i] = -INFINITY;
+        mb = fmaxf(mb, sv[i]);
+      }
+      const float m_new = fmaxf(m, mb);
+      const float corr = fast_exp2(m - m_new);  // 0 on the first block (m = -inf)
+      float sum = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = fast_exp2(sv[2 * i] - m_new), p1 = fast_exp2(sv[2 * i + 1] - m_new);
+        sum += p0 + p1;
+        half2 h2 = __floats2half2_rn(p0, p1);
+        pk[i] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      l = l * corr + sum;
+      // P and O are free once the previous block's P V MMA has completed
+      if (j > 0) {
+        if (!mbar_wait_warp(&o_done, (j - 1) & 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // rescale O when the running max of any row of this warp grew (rows whose max did not grow
+        // have corr == 1 exactly); the TMEM accesses need the whole warp
+        if (__any_sync(0xffffffffu, m_new > m)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t u[16];
+            tc_ld16(lane_base + 64 + c * 16, u);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
+            tc_st16(lane_base + 64 + c * 16, u);
+          }
+          tc_wait_st();
+        }
+      }
+      m = m_new;
+      // P row r: 8 chunks of 16 bytes, chunk c at r * 128 + ((c ^ (r & 7)) * 16) (128B swizzle)
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(ps + r * 128 + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_proxy_async_shared();  // generic-proxy P stores -> tensor-core reads
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full);
+    }
+    if (ok && nkb > 0 && mbar_wait_warp(&o_done, (nkb - 1) & 1u)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const int row = q0 + r;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[16];
+        tc_ld16(lane_base + 64 + c * 16, u);
+        tc_wait_ld();
+        if (row < seq) {
+          uint4 w[2];
+          half2* h = reinterpret_cast<half2*>(w);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            h[i] = __floats2half2_rn(__uint_as_float(u[2 * i]) * inv, __uint_as_float(u[2 * i + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ldo + head * 64 + c * 16);
+          dst[0] = w[0];
+          dst[1] = w[1];
+        }
+      }
     } else {
-      cp_async_wait<0>();
+      enc_flag(FW_DEVERR_TIMEOUT);
     }
-    __syncthreads();
-    if (kb == 0) {
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int mi = lane >> 3, r = lane & 7;
-        const int row = warp * 16 + r + ((mi & 1) << 3);
-        const int chunk = 2 * kk + (mi >> 1);
-        ldsm_x4(qs_base + swz(row, chunk), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
-      }
-    }
-    const uint32_t kbase = smem_u32(ks[buf]);
-    const uint32_t vbase = smem_u32(vs[buf]);
-    float s[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        const int mi = lane >> 3, r = lane & 7;
-        const int key = j * 8 + ((mi >> 1) << 3) + r;
-        const int chunk = 2 * kk + (mi & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + swz(key, chunk), b0, b1, b2, b3);
-        mma16816(s[j], qa[kk], b0, b1);
-        mma16816(s[j + 1], qa[kk], b2, b3);
-      }
-    }
-    // mask keys beyond the sequence, then the online softmax update
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int key = kb * kEncK + j * 8 + 2 * t;
-      if (key >= seq) s[j][0] = s[j][2] = -INFINITY;
-      if (key + 1 >= seq) s[j][1] = s[j][3] = -INFINITY;
-      mx[0] = fmaxf(mx[0], fmaxf(s[j][0], s[j][1]));
-      mx[1] = fmaxf(mx[1], fmaxf(s[j][2], s[j][3]));
-    }
-    float alpha[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
-      const float mnew = fmaxf(mrow[i], mx[i]);
-      alpha[i] = exp2f((mrow[i] - mnew) * kLog2e);
-      mrow[i] = mnew;
-      lrow[i] *= alpha[i];
-    }
-    const float mb0 = mrow[0] * kLog2e, mb1 = mrow[1] * kLog2e;
-    uint32_t pa[4][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float p0 = exp2f(fmaf(s[j][0], kLog2e, -mb0));
-      const float p1 = exp2f(fmaf(s[j][1], kLog2e, -mb0));
-      const float p2 = exp2f(fmaf(s[j][2], kLog2e, -mb1));
-      const float p3 = exp2f(fmaf(s[j][3], kLog2e, -mb1));
-      lrow[0] += p0 + p1;
-      lrow[1] += p2 + p3;
-      pa[j >> 1][(j & 1) * 2 + 0] = pack_half2(p0, p1);
-      pa[j >> 1][(j & 1) * 2 + 1] = pack_half2(p2, p3);
-      o[j][0] *= alpha[0];
-      o[j][1] *= alpha[0];
-      o[j][2] *= alpha[1];
-      o[j][3] *= alpha[1];
-    }
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int n = 0; n < 8; n += 2) {
-        const int mi = lane >> 3, r = lane & 7;
-        const int key = kk * 16 + ((mi & 1) << 3) + r;
-        const int chunk = n + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vbase + swz(key, chunk), b0, b1, b2, b3);
-        mma16816(o[n], pa[kk], b0, b1);
-        mma16816(o[n + 1], pa[kk], b2, b3);
-      }
-    }
-    __syncthreads();
   }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 1);
-    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 2);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
   }
-  const float inv0 = 1.f / lrow[0], inv1 = 1.f / lrow[1];
-  const int r0 = q0 + warp * 16 + g;
-#pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const int col = head * 64 + n * 8 + 2 * t;
-    if (r0 < seq)
-      *reinterpret_cast<half2*>(out + static_cast<size_t>(r0) * (gridDim.y * 64) + col) =
-          __floats2half2_rn(o[n][0] * inv0, o[n][1] * inv0);
-    if (r0 + 8 < seq)
-      *reinterpret_cast<half2*>(out + static_cast<size_t>(r0 + 8) * (gridDim.y * 64) + col) =
-          __floats2half2_rn(o[n][2] * inv1, o[n][3] * inv1);
+}
+
+// V^T [heads * 64, ldv] (keys contiguous) from the v columns of a [seq, ld] q|k|v buffer, for the
+// stand-alone attention entry point (the encoder writes V^T straight from the QKV GEMM epilogue).
+__global__ void __launch_bounds__(256) transpose_v_kernel(const half* __restrict__ qkv, int64_t ld, int vcol,
+                                                          half* __restrict__ vt, int64_t ldv, int seq, int cols) {
+  __shared__ half tile[32][33];
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  pdl_wait();
+  pdl_trigger();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int t = t0 + i, c = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (t < seq && c < cols) ? qkv[static_cast<size_t>(t) * ld + vcol + c] : __float2half(0.f);
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, t = t0 + threadIdx.x;
+    if (c < cols && t < seq) vt[static_cast<size_t>(c) * ldv + t] = tile[threadIdx.x][i];
   }
 }
 
@@ -724,9 +821,11 @@ static int check_epi(const GemmEpi& ep, int K) {
   FW_REQUIRE(ep.C != nullptr, FW_ERR_NULL, "gemm: C is required");
   FW_REQUIRE(ep.M > 0 && ep.N > 0 && ep.N % 64 == 0 && K > 0 && K % 64 == 0, FW_ERR_SHAPE,
              "gemm: need M > 0, N %% 64 == 0, K %% 64 == 0 (M=%d N=%d K=%d)", ep.M, ep.N, K);
-  FW_REQUIRE(ep.mode >= FW_EPI_BIAS && ep.mode <= FW_EPI_BIAS_SCALE, FW_ERR_ARG, "gemm: unknown epilogue %d", ep.mode);
-  FW_REQUIRE((ep.mode != FW_EPI_BIAS_RESID && ep.mode != FW_EPI_GELU_POS) || ep.R != nullptr, FW_ERR_NULL,
-             "gemm: this epilogue needs R");
+  FW_REQUIRE(ep.mode >= FW_EPI_BIAS && ep.mode <= FW_EPI_QKV_VT, FW_ERR_ARG, "gemm: unknown epilogue %d", ep.mode);
+  FW_REQUIRE((ep.mode != FW_EPI_BIAS_RESID && ep.mode != FW_EPI_GELU_POS && ep.mode != FW_EPI_QKV_VT) || ep.R != nullptr,
+             FW_ERR_NULL, "gemm: this epilogue needs R");
+  FW_REQUIRE(ep.mode != FW_EPI_QKV_VT || (ep.N % 48 == 0 && ep.vt_col == ep.N / 3 * 2 && ep.ldr >= ep.M), FW_ERR_SHAPE,
+             "gemm: FW_EPI_QKV_VT needs N %% 48 == 0 and ldr >= M");
   FW_REQUIRE(ep.mode == FW_EPI_CROSS_KV || (ep.ldc >= ep.N && ep.ldc % 8 == 0), FW_ERR_SHAPE,
              "gemm: ldc must be >= N and a multiple of 8");
   FW_REQUIRE(aligned16(ep.C) && (ep.bias == nullptr || aligned16(ep.bias)) && (ep.R == nullptr || aligned16(ep.R)),
@@ -775,14 +874,26 @@ static int run_layernorm(const void* x, const void* g, const void* b, void* y, i
   return launch_status(e, "layernorm_rows");
 }
 
-static int run_attention(const void* qkv, int64_t ld, int kcol, int vcol, void* out, int seq, int heads,
-                         cudaStream_t s, bool pdl) {
-  FW_REQUIRE(qkv && out, FW_ERR_NULL, "encoder_attention: qkv and out are required");
-  FW_REQUIRE(seq > 0 && heads > 0 && ld % 8 == 0 && kcol % 8 == 0 && vcol % 8 == 0, FW_ERR_SHAPE,
-             "encoder_attention: bad sizes");
-  FW_REQUIRE(aligned16(qkv) && aligned16(out), FW_ERR_ALIGN, "encoder_attention: 16-byte alignment required");
-  cudaError_t e = launch(enc_attention_kernel, dim3((seq + kEncQ - 1) / kEncQ, heads), dim3(256), 0, s, pdl,
-                         static_cast<const half*>(qkv), ld, kcol, vcol, static_cast<half*>(out), seq);
+// Attention over q at columns h*64 and k at kcol + h*64 of qkv [seq, ld], and V^T [heads*64, ldv].
+static int run_attention(const void* qkv, int64_t ld, int kcol, const void* vt, int64_t ldv, void* out, int seq,
+                         int heads, cudaStream_t s, bool pdl) {
+  FW_REQUIRE(qkv && vt && out, FW_ERR_NULL, "encoder_attention: qkv, vt and out are required");
+  FW_REQUIRE(seq > 0 && heads > 0 && ld % 8 == 0 && kcol % 8 == 0 && kcol >= heads * 64 &&
+                 ld >= kcol + heads * 64 && ldv % 8 == 0 && ldv >= seq,
+             FW_ERR_SHAPE, "encoder_attention: bad sizes");
+  FW_REQUIRE(aligned16(qkv) && aligned16(vt) && aligned16(out), FW_ERR_ALIGN,
+             "encoder_attention: 16-byte alignment required");
+  CUtensorMap tqk, tvt;
+  int rc = make_map_2d(&tqk, qkv, static_cast<uint64_t>(kcol + heads * 64), static_cast<uint64_t>(seq),
+                       static_cast<uint64_t>(ld), 64);
+  if (rc) return rc;
+  rc = make_map_2d(&tvt, vt, static_cast<uint64_t>(seq), static_cast<uint64_t>(heads * 64), static_cast<uint64_t>(ldv),
+                   64);
+  if (rc) return rc;
+  cudaError_t e = ensure_smem(enc_attn_tc_kernel, kAttnSmem);
+  if (e == cudaSuccess)
+    e = launch(enc_attn_tc_kernel, dim3((seq + kAttnQ - 1) / kAttnQ, heads), dim3(192), kAttnSmem, s, pdl, tqk, tvt,
+               kcol, static_cast<half*>(out), heads * 64, seq);
   return launch_status(e, "encoder_attention");
 }
 
@@ -806,7 +917,7 @@ int fw_gemm_f16(const void* A, int64_t lda, const void* B, int64_t ldb, const vo
                 const void* R, int64_t ldr, int M, int N, int K, int epilogue, float scale, int scale_cols,
                 fw_stream_t stream) {
   GemmEpi ep{static_cast<const half*>(bias), static_cast<half*>(C), ldc, static_cast<const half*>(R), ldr, M, N,
-             epilogue, scale, scale_cols};
+             epilogue, scale, scale_cols, epilogue == FW_EPI_QKV_VT ? N / 3 * 2 : 0};
   return run_gemm(A, lda, B, ldb, K, ep, static_cast<cudaStream_t>(stream), false);
 }
 
@@ -823,8 +934,17 @@ int fw_layernorm_rows(const void* x, const void* g, const void* b, void* y, int 
 }
 
 int fw_encoder_attention(const void* qkv, int64_t ld, int kcol, int vcol, void* out, int seq, int heads,
-                         fw_stream_t stream) {
-  return run_attention(qkv, ld, kcol, vcol, out, seq, heads, static_cast<cudaStream_t>(stream), false);
+                         void* vt_scratch, fw_stream_t stream) {
+  FW_REQUIRE(qkv && out && vt_scratch, FW_ERR_NULL, "encoder_attention: qkv, out and vt_scratch are required");
+  FW_REQUIRE(seq > 0 && heads > 0 && vcol % 8 == 0 && ld >= vcol + heads * 64, FW_ERR_SHAPE,
+             "encoder_attention: bad sizes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t ldv = (seq + 7) / 8 * 8;
+  cudaError_t e = launch(transpose_v_kernel, dim3((seq + 31) / 32, heads * 2), dim3(32, 8), 0, s, false,
+                         static_cast<const half*>(qkv), ld, vcol, static_cast<half*>(vt_scratch), ldv, seq, heads * 64);
+  int rc = launch_status(e, "encoder_attention_transpose");
+  if (rc) return rc;
+  return run_attention(qkv, ld, kcol, vt_scratch, ldv, out, seq, heads, s, false);
 }
 
 int fw_encoder_forward(const fw_encoder_t* e, fw_stream_t stream) {
@@ -840,6 +960,9 @@ int fw_encoder_forward(const fw_encoder_t* e, fw_stream_t stream) {
   half* qkv = static_cast<half*>(e->qkv);
   half* attn = static_cast<half*>(e->attn);
   half* ffn = static_cast<half*>(e->ffn);
+  half* vt = static_cast<half*>(e->vt);
+  const int64_t ldv = (T + 7) / 8 * 8;
+  FW_REQUIRE(vt != nullptr, FW_ERR_NULL, "encoder_forward: vt is required");
   int rc;
   // conv1 + GELU -> rows 1..F of conv1_out (rows 0 and F+1 stay zero)
   GemmEpi ep{static_cast<const half*>(e->conv1_b), conv1_out + kHidden, kHidden, nullptr, 0, F, kHidden,
@@ -858,10 +981,10 @@ int fw_encoder_forward(const fw_encoder_t* e, fw_stream_t stream) {
     const fw_encoder_layer_t& L = e->layers[l];
     const void* next_qkv = l + 1 < e->n_layers ? e->layers[l + 1].qkv_w : nullptr;
     if ((rc = run_layernorm(x, L.ln1_g, L.ln1_b, y, T, kHidden, e->eps, s, true))) return rc;
-    ep = GemmEpi{static_cast<const half*>(L.qkv_b), qkv, 3 * kHidden, nullptr, 0, T, 3 * kHidden,
-                 FW_EPI_BIAS_SCALE, 0.125f, kHidden};
+    ep = GemmEpi{static_cast<const half*>(L.qkv_b), qkv, 3 * kHidden, vt, ldv, T, 3 * kHidden,
+                 FW_EPI_QKV_VT, 0.125f, kHidden, 2 * kHidden};
     if ((rc = run_gemm(y, kHidden, L.qkv_w, kHidden, kHidden, ep, s, true, L.out_w, kSq))) return rc;
-    if ((rc = run_attention(qkv, 3 * kHidden, kHidden, 2 * kHidden, attn, T, e->heads, s, true))) return rc;
+    if ((rc = run_attention(qkv, 3 * kHidden, kHidden, vt, ldv, attn, T, e->heads, s, true))) return rc;
     ep = GemmEpi{static_cast<const half*>(L.out_b), x, kHidden, x, kHidden, T, kHidden, FW_EPI_BIAS_RESID, 1.f, 0};
     if ((rc = run_gemm(attn, kHidden, L.out_w, kHidden, kHidden, ep, s, true, L.fc1_w, kFf))) return rc;
     if ((rc = run_layernorm(x, L.ln2_g, L.ln2_b, y, T, kHidden, e->eps, s, true))) return rc;

@@ -206,11 +206,15 @@ class Ext:
         _lib.call('fw_layernorm_rows', _ptr(x), _ptr(g), _ptr(b), _ptr(y), x.size(0), x.size(1), float(eps),
                   _stream())
 
-    def encoder_attention(self, qkv, out, heads, kcol=HIDDEN, vcol=2 * HIDDEN):
+    def encoder_attention(self, qkv, out, heads, kcol=HIDDEN, vcol=2 * HIDDEN, vt=None):
+        """vt: optional fp16 scratch [heads * 64, round_up(seq, 8)] for V transposed (allocated if None)."""
         _check_half(qkv, 'qkv')
         _check_half(out, 'out')
+        if vt is None:
+            vt = torch.empty(int(heads) * 64, -(-qkv.size(0) // 8) * 8, dtype=torch.float16, device=qkv.device)
+        _check_half(vt, 'vt')
         _lib.call('fw_encoder_attention', _ptr(qkv), qkv.stride(0), int(kcol), int(vcol), _ptr(out), qkv.size(0),
-                  int(heads), _stream())
+                  int(heads), _ptr(vt), _stream())
 
     def decoder_step(self, desc, steps=1):
         _lib.call('fw_decoder_step', ctypes.byref(desc), int(steps), _stream())

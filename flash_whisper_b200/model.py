@@ -130,6 +130,7 @@ class CustomModel:
         self.eattn = torch.zeros(T, d, dtype=half, device=dev)
         self.effn = torch.zeros(T, dims.ffn, dtype=half, device=dev)
         self.enc_out = torch.zeros(T, d, dtype=half, device=dev)
+        self.evt = torch.zeros(d, -(-T // 8) * 8, dtype=half, device=dev)  # V^T of the encoder attention
         self.tokens_host = torch.zeros(self.max_pos, dtype=torch.long).pin_memory()
 
         self.dec_desc = self._decoder_desc()
@@ -191,7 +192,7 @@ class CustomModel:
         desc.cross_w, desc.cross_b = _p(self.dec.cross_w), _p(self.dec.cross_b)
         desc.conv1_out, desc.x, desc.y = _p(self.conv1_out), _p(self.ex), _p(self.ey)
         desc.qkv, desc.attn, desc.ffn = _p(self.eqkv), _p(self.eattn), _p(self.effn)
-        desc.enc_out, desc.cross_kv = _p(self.enc_out), _p(self.cross_kv)
+        desc.enc_out, desc.cross_kv, desc.vt = _p(self.enc_out), _p(self.cross_kv), _p(self.evt)
         return desc
 
     # ---- stages (eager; also what the graphs record) -----------------------------------------

@@ -194,6 +194,8 @@ int fw_log_mel(const float* wave, int batch, int n_samples, const float* filters
 #define FW_EPI_GELU_POS 3     /* C = fp16(fp16(gelu(fp16(acc + bias))) + R[row]) (conv2 + positions) */
 #define FW_EPI_CROSS_KV 4     /* cross K/V scatter into [layers, 2, heads, M, 64] */
 #define FW_EPI_BIAS_SCALE 5   /* C = fp16(fp16(acc + bias) * scale) for columns < scale_cols */
+#define FW_EPI_QKV_VT 6       /* as FW_EPI_BIAS_SCALE for columns n < 2N/3 (q | k); the last third (v)
+                                 is written transposed instead: R[(n - 2N/3) * ldr + m] */
 
 /* C[M, N] = epilogue(A[M, K] . B[N, K]^T + bias[N]) on tcgen05 tensor cores, fp16 in, fp32
  * accumulate in TMEM. lda/ldb/ldc/ldr are row strides in elements. K % 64 == 0, N % 64 == 0;
@@ -217,10 +219,12 @@ int fw_conv1d_k3_f16(const void* X, int C, int rows_padded, int stride, const vo
 int fw_layernorm_rows(const void* x, const void* g, const void* b, void* y, int rows, int cols, float eps,
                       fw_stream_t stream);
 
-/* Bidirectional multi-head attention for the encoder. qkv fp16 [seq, ld] holding pre-scaled q at
- * column h*64, k at kcol + h*64 and v at vcol + h*64; out fp16 [seq, heads*64]. */
+/* Bidirectional multi-head attention for the encoder (tcgen05, TMEM accumulators). qkv fp16
+ * [seq, ld] holding pre-scaled q at column h*64, k at kcol + h*64 and v at vcol + h*64; out fp16
+ * [seq, heads*64]. vt_scratch: fp16 [heads*64, round_up(seq, 8)] caller-owned scratch that receives
+ * V transposed. Replaces the SDPA attention of the HF WhisperEncoderLayer. */
 int fw_encoder_attention(const void* qkv, int64_t ld, int kcol, int vcol, void* out, int seq, int heads,
-                         fw_stream_t stream);
+                         void* vt_scratch, fw_stream_t stream);
 
 #define FW_MAX_ENC_LAYERS 32
 typedef struct {
@@ -245,6 +249,7 @@ typedef struct {
                                       [n_pos,5120] */
   void* enc_out;                   /* fp16 [n_pos, 1280] final-LN output */
   void* cross_kv;                  /* fp16 [n_dec_layers, 2, heads, n_pos, 64] */
+  void* vt;                        /* fp16 [heads*64, round_up(n_pos, 8)] V^T scratch */
 } fw_encoder_t;
 
 /* mel -> encoder states -> cross K/V for every decoder layer (custom/model.py:143-147). */

@@ -62,6 +62,22 @@ def test_gemm_epilogues(ext):
     _close(c, ref.half())
 
 
+def test_gemm_qkv_transposed_v_epilogue(ext):
+    m, n, k = 1500, 3840, 1280
+    a, b, bias = _rand(m, k, seed=21), _rand(n, k, scale=k ** -0.5, seed=22), _rand(n, scale=0.1, seed=23)
+    acc = (a.float() @ b.float().T + bias.float()).half().float()
+    c = torch.full((m, n), 7.0, device='cuda', dtype=torch.float16)
+    ldv = 1504
+    vt = torch.zeros(1280, ldv, device='cuda', dtype=torch.float16)
+    ext.gemm(a, b, bias, c, _lib.FW_EPI_QKV_VT, r=vt, scale=0.125, scale_cols=1280)
+    ref = acc.clone()
+    ref[:, :1280] *= 0.125
+    _close(c[:, :2560], ref[:, :2560].half())
+    assert bool((c[:, 2560:] == 7.0).all()), 'v columns must not be written to C'
+    _close(vt[:, :m], acc[:, 2560:].T.contiguous().half())
+    assert float(vt[:, m:].abs().max()) == 0.0
+
+
 def test_gemm_cross_kv_scatter(ext):
     m, layers, heads = 1500, 4, 20
     n, k = layers * 2 * 1280, 1280
