@@ -9,7 +9,7 @@ in this package's CUDA kernels, recorded into CUDA graphs:
     final LN, cross-K/V GEMM scattered straight into the decoder's cross cache);
   * prompt graph: state reset + the 4 prompt steps (prompt ids are read on the device, so the
     host never writes `cur` between steps as custom/model.py:199-207 does);
-  * chunk graph: CHUNK decode steps (fw_decoder_step, 34 PDL-chained launches per token).
+  * chunk graph: CHUNK decode steps (fw_decoder_step, 17 PDL-chained launches per token).
 
 The host reads tokens back once per chunk, one chunk behind the GPU, and stops at EOS like
 custom/model.py:210-215; with `max_new_tokens` and `stop_at_eos=False` it replays all chunks and
