@@ -319,13 +319,18 @@ __device__ __forceinline__ void attn_unit64(const half* ks, const half* vs, int 
   e = warp_sum(e);
   if (lane == 0) U.red[2 + wa] = e;
   unit_sync(sync_id);
-  // value accumulation: warp wa owns residues wa and wa + 2
+  // value accumulation: warp wa owns residues wa and wa + 2, keys i = wa + 4k in order. The loop
+  // has a compile-time trip count so the shared-memory loads are issued ahead of the fma chains.
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-  for (int i = wa; i < n; i += 4) {
-    const float2 v0 = __half22float2(reinterpret_cast<const half2*>(vs + i * kHeadDim)[lane]);
-    const float p0 = U.sc[i];
-    acc0.x = fmaf(p0, v0.x, acc0.x);
-    acc0.y = fmaf(p0, v0.y, acc0.y);
+#pragma unroll
+  for (int k = 0; k < kSplitKeys / 4; ++k) {
+    const int i = wa + 4 * k;
+    if (i < n) {
+      const float2 v0 = __half22float2(reinterpret_cast<const half2*>(vs + i * kHeadDim)[lane]);
+      const float p0 = U.sc[i];
+      acc0.x = fmaf(p0, v0.x, acc0.x);
+      acc0.y = fmaf(p0, v0.y, acc0.y);
+    }
     if (i + 2 < n) {
       const float2 v1 = __half22float2(reinterpret_cast<const half2*>(vs + (i + 2) * kHeadDim)[lane]);
       const float p1 = U.sc[i + 2];
@@ -743,14 +748,17 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   // exp(m_s - m) are computed one per thread, then the sums run in split order ----
   if (tid < splits) {
     float m = -INFINITY;
-    for (int s = 0; s < splits; ++s) m = fmaxf(m, sm_m[s]);
+#pragma unroll
+    for (int s = 0; s < S::kSlots; ++s)
+      if (s < splits) m = fmaxf(m, sm_m[s]);
     sm_w[tid] = sm_l[tid] > 0.f ? __expf(sm_m[tid] - m) : 0.f;
   }
   __syncthreads();
   if (tid < kHeadDim) {
     float num = 0.f, den = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      if (sm_l[s] > 0.f) {
+#pragma unroll
+    for (int s = 0; s < S::kSlots; ++s) {
+      if (s < splits && sm_l[s] > 0.f) {
         const float w = sm_w[s];
         num = fmaf(sm_acc[s][tid], w, num);
         den = fmaf(sm_l[s], w, den);
@@ -767,20 +775,27 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   if (!mbar_wait(&bar_o, 0)) flag_error(FW_DEVERR_TIMEOUT);
   if (tid < kOutRows) {
     const uint4* wr = reinterpret_cast<const uint4*>(wout + tid * kHeadDim);
-    float acc = 0.f;
+    const float4* o4 = reinterpret_cast<const float4*>(os);
+    float acc2[2] = {0.f, 0.f};  // two chains: even and odd steps of the rotated chunk order
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int c = (j + tid) & 7;  // rotation keeps the 16-byte shared loads conflict-free
       const uint4 wv = wr[c];
+      const float4 oa = o4[2 * c], ob = o4[2 * c + 1];
       const half2* w2 = reinterpret_cast<const half2*>(&wv);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(w2[e]);
-        acc = fmaf(f.x, os[8 * c + 2 * e], acc);
-        acc = fmaf(f.y, os[8 * c + 2 * e + 1], acc);
-      }
+      const float2 f0 = __half22float2(w2[0]), f1 = __half22float2(w2[1]);
+      const float2 f2 = __half22float2(w2[2]), f3 = __half22float2(w2[3]);
+      float& a = acc2[j & 1];
+      a = fmaf(f0.x, oa.x, a);
+      a = fmaf(f0.y, oa.y, a);
+      a = fmaf(f1.x, oa.z, a);
+      a = fmaf(f1.y, oa.w, a);
+      a = fmaf(f2.x, ob.x, a);
+      a = fmaf(f2.y, ob.y, a);
+      a = fmaf(f3.x, ob.z, a);
+      a = fmaf(f3.y, ob.w, a);
     }
-    __stcg(p.part + static_cast<size_t>(head) * kHidden + row0 + tid, acc);
+    __stcg(p.part + static_cast<size_t>(head) * kHidden + row0 + tid, acc2[0] + acc2[1]);
   }
 
   // ---- 5. residual update by the last CTA of this row block ----
