@@ -148,6 +148,10 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 __device__ __forceinline__ void l2_prefetch(const void* p, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void l2_prefetch_hint(const void* p, unsigned bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p), "r"(bytes), "l"(policy)
+               : "memory");
+}
 
 // Split cluster barrier: every thread of every CTA of the cluster arrives, then waits. A CTA may
 // access another CTA's shared memory only after a completed barrier phase that the other CTA

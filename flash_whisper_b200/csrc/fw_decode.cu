@@ -598,6 +598,8 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     pos_known = true;
   }
 
+  // Weights and the cross cache are read once per step: streamed with L2 evict-first.
+  const uint64_t stream_policy = policy_evict_first();
   if (tid == 0) {
     mbar_init(&bar_w, 1);
     mbar_init(&bar_kv, 1);
@@ -605,8 +607,8 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     mbar_fence_init();
     mbar_arrive_expect_tx(&bar_w, S::kProjBytes);
     for (int r = 0; r < S::kProjRows; ++r)
-      bulk_g2s(wproj + r * kHidden, p.w + static_cast<size_t>(proj_row(rank * S::kProjRows + r)) * kHidden,
-               kHidden * 2, &bar_w);
+      bulk_g2s_stream(wproj + r * kHidden, p.w + static_cast<size_t>(proj_row(rank * S::kProjRows + r)) * kHidden,
+                      kHidden * 2, &bar_w, stream_policy);
     // K/V rows of this CTA's splits: the keys below the attention length (all of them while the
     // length is not yet known; rows past it are fetched but not used). A unit that attends over
     // n > 0 keys after the wait always had its rows requested here, so it may wait on bar_kv.
@@ -623,13 +625,21 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
         if (nkv[u] == 0) continue;
         const int begin = (rank * S::kUnits + u) * kSplitKeys;
         const unsigned bytes = static_cast<unsigned>(nkv[u]) * kHeadDim * 2;
-        bulk_g2s(kvs + (2 * u) * kSplitKeys * kHeadDim, kh + static_cast<size_t>(begin) * kHeadDim, bytes, &bar_kv);
-        bulk_g2s(kvs + (2 * u + 1) * kSplitKeys * kHeadDim, vh + static_cast<size_t>(begin) * kHeadDim, bytes,
-                 &bar_kv);
+        if (kSelf) {  // the self cache is small and rewritten every step: default policy
+          bulk_g2s(kvs + (2 * u) * kSplitKeys * kHeadDim, kh + static_cast<size_t>(begin) * kHeadDim, bytes, &bar_kv);
+          bulk_g2s(kvs + (2 * u + 1) * kSplitKeys * kHeadDim, vh + static_cast<size_t>(begin) * kHeadDim, bytes,
+                   &bar_kv);
+        } else {
+          bulk_g2s_stream(kvs + (2 * u) * kSplitKeys * kHeadDim, kh + static_cast<size_t>(begin) * kHeadDim, bytes,
+                          &bar_kv, stream_policy);
+          bulk_g2s_stream(kvs + (2 * u + 1) * kSplitKeys * kHeadDim, vh + static_cast<size_t>(begin) * kHeadDim,
+                          bytes, &bar_kv, stream_policy);
+        }
       }
     }
     // the output-projection slice is copied into shared memory after step 1; warm it in L2 now
-    l2_prefetch(p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes);
+    l2_prefetch_hint(p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes,
+                     stream_policy);
   }
   // LayerNorm parameters and biases are weights: loaded before the wait, into registers
   constexpr int kRowsPerWarp = (S::kProjRows + 7) / 8;
@@ -702,7 +712,8 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   if (tid == 0) {  // every thread of this CTA is past its reads of the projection rows
     fence_proxy_async_shared();
     mbar_arrive_expect_tx(&bar_o, S::kOutBytes);
-    bulk_g2s(wout, p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes, &bar_o);
+    bulk_g2s_stream(wout, p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes,
+                    &bar_o, stream_policy);
   }
 
   // ---- 2. attention splits ----
@@ -825,12 +836,13 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
 // ---------------------------------------------------------------------------------------------
 // LM head: fused (optional final LayerNorm) + GEMV over the vocab + argmax (+ optional finalize).
 // One CTA per SM owns a contiguous range of vocab rows; each of its 8 warps streams its own
-// contiguous share through a private ring of kLmSlots shared-memory slots (kLmSlotRows rows each)
+// contiguous share through a private ring of kLmSlots shared-memory slots (kLmSlotRows rows each,
+// 160 KB per CTA)
 // fed by bulk async copies issued by the warp's lane 0. Warps never wait for one another inside the
 // loop, so a slot is refilled as soon as its warp has consumed it and the bytes in flight stay high
 // while other warps compute; two rows per slot are dotted together to overlap their latency. The
 // first slots are requested before griddepcontrol.wait.
-constexpr int kLmSlots = 2;
+constexpr int kLmSlots = 4;
 constexpr int kLmSlotRows = 2;
 constexpr int kLmSlotBytes = kLmSlotRows * kHidden * 2;
 constexpr int kLmSmem = 8 * kLmSlots * kLmSlotBytes;
@@ -1041,7 +1053,8 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
     if (nr > 0) {
       mbar_arrive_expect_tx(&bar, static_cast<unsigned>(nr) * kHidden * 2);
       for (int r = 0; r < nr; ++r)
-        bulk_g2s(ws + r * kHidden, p.w + static_cast<size_t>(r0 + r) * kHidden, kHidden * 2, &bar);
+        bulk_g2s_stream(ws + r * kHidden, p.w + static_cast<size_t>(r0 + r) * kHidden, kHidden * 2, &bar,
+                        policy_evict_first());
     }
   }
   float g[5], be[5], bias[kRowsPerWarp];
@@ -1129,7 +1142,8 @@ __global__ void __launch_bounds__(kResidThreads) gemv_residual_kernel(GemvParams
     if (nr > 0) {
       mbar_arrive_expect_tx(&bar, static_cast<unsigned>(nr) * k * 2);
       for (int r = 0; r < nr; ++r)
-        bulk_g2s(smem + static_cast<size_t>(r) * k * 2, p.w + static_cast<size_t>(r0 + r) * k, k * 2, &bar);
+        bulk_g2s_stream(smem + static_cast<size_t>(r) * k * 2, p.w + static_cast<size_t>(r0 + r) * k, k * 2, &bar,
+                        policy_evict_first());
     }
   }
   const bool owner = tid < nr;  // thread r finishes row r
