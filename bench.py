@@ -18,6 +18,12 @@ ranks timing reduction outside the timed region.
 
 --impl reference times the reference's own CPU path (custom/pytorch_model.py's greedy loop restated
 for CPU fp32 by oracle/hf_cpu.py) on the host cores on the same config, one bounded sample per step.
+
+--workload clips256 runs BASELINE config 4 instead: 256 clips (audio seed i, lengths uniform in
+[5, 30] s, zero-padded to 30 s) with round(7.5 tokens/s x seconds) forced tokens each, split over the
+ranks by a static longest-first greedy partition on the forced-token count; the metric is the
+whole-box throughput in audio-seconds per second (total audio / max-over-ranks device time, strong
+scaling: the 256 clips are the same for every N).
 """
 
 import argparse
@@ -37,6 +43,8 @@ sys.path.insert(0, str(ROOT))
 
 SECONDS = 30.0
 N_TOKENS = 224
+N_CLIPS = 256
+TOKENS_PER_SECOND = 7.5
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one lm_head_kernel launch (ncu --set full, see
 # profiles/lm_head_argmax_decode_step.txt): 132.92 MB read + 6.13 MB written (evicted dirty L2 lines
@@ -101,6 +109,30 @@ class ClockSampler:
         if not sm:
             return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unavailable']}
         return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def clip_set(n=N_CLIPS):
+    """BASELINE config 4 clips: (audio seed, seconds, forced tokens); seconds ~ U[5, 30] from
+    numpy default_rng(0), quantised to whole samples; tokens = round(7.5 * seconds)."""
+    secs = np.random.default_rng(0).uniform(5.0, 30.0, size=n)
+    out = []
+    for i, sec in enumerate(secs):
+        samples = int(round(sec * 16000))
+        out.append((i, samples / 16000.0, int(round(TOKENS_PER_SECOND * samples / 16000.0))))
+    return out
+
+
+def partition(clips, world):
+    """Static longest-first greedy partition of clips over ranks by forced-token count (ties go to the
+    lower rank, then to the lower clip index); returns per-rank lists of clip indices in run order."""
+    order = sorted(range(len(clips)), key=lambda i: (-clips[i][2], i))
+    load = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        parts[r].append(i)
+        load[r] += clips[i][2]
+    return parts
 
 
 def decode_bytes_per_token(dims, length):
@@ -221,7 +253,7 @@ def bench_ours(args, rank, world, local_rank):
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     reps = max(3, args.steps)
     mel_ms = enc_ms = dec_ms = 0.0
-    n_chunks = -(-(N_TOKENS - 1) // model.chunk)
+    dec_steps = N_TOKENS - 1  # the prompt's last step yields the first token
     for _ in range(reps):
         ev[0].record(stream)
         model.run_mel()
@@ -230,14 +262,12 @@ def bench_ours(args, rank, world, local_rank):
         ev[2].record(stream)
         model.run_prompt()
         ev[3].record(stream)
-        for _ in range(n_chunks):
-            model.run_chunk()
+        model.run_steps(dec_steps)
         ev[4].record(stream)
         torch.cuda.synchronize()
         mel_ms += ev[0].elapsed_time(ev[1]) / reps
         enc_ms += ev[1].elapsed_time(ev[2]) / reps
         dec_ms += ev[3].elapsed_time(ev[4]) / reps
-    dec_steps = n_chunks * model.chunk
     us_per_token = maxed(dec_ms * 1e3 / dec_steps)
 
     # (3) LM-head kernel alone (the largest single kernel of the decode step), same stream
@@ -315,6 +345,104 @@ def bench_ours(args, rank, world, local_rank):
     return 0
 
 
+@torch.inference_mode()
+def bench_clips(args, rank, world, local_rank):
+    """the 256-clip stream, statically partitioned over the ranks."""
+    from flash_whisper_b200.audio import synthetic_audio
+    from flash_whisper_b200.model import CustomModel
+    from flash_whisper_b200.weights import TURBO, random_state_dict
+
+    torch.cuda.set_device(local_rank)
+    dims = TURBO
+    model = CustomModel(state_dict=random_state_dict(0, dims), dims=dims, selftest=False)
+    clips = clip_set()
+    mine = partition(clips, world)[rank]
+    audios = {i: synthetic_audio(clips[i][0], clips[i][1]) for i in mine}
+    waves = torch.zeros(max(1, len(mine)), 480000, dtype=torch.float32, device='cuda')  # resident in HBM
+    for j, i in enumerate(mine):
+        waves[j, :audios[i].size] = torch.from_numpy(audios[i]).cuda()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def reduce(x, op):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device='cuda')
+        torch.distributed.all_reduce(t, op=op)
+        return float(t)
+
+    for j, i in enumerate(mine[:max(args.warmup, 3)]):
+        model.wave.copy_(waves[j])
+        model.decode_device(clips[i][2])
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for j, i in enumerate(mine):
+            model.wave.copy_(waves[j])
+            model.decode_device(clips[i][2])
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    max_ms = reduce(e0.elapsed_time(e1), torch.distributed.ReduceOp.MAX if world > 1 else None)
+    total_audio = sum(c[1] for c in clips)
+    total_tokens = sum(c[2] for c in clips)
+    launches = reduce(sum(2 + (2 + 7 * dims.encoder_layers + 2) + (4 * dims.decoder_layers + 1) * (3 + clips[i][2])
+                          for i in mine), torch.distributed.ReduceOp.SUM if world > 1 else None)
+
+    # end to end through the public API: host audio -> host token ids, same partition
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in mine:
+        model.transcribe(audios[i], max_new_tokens=clips[i][2], stop_at_eos=False)
+    e2e_s = reduce(time.perf_counter() - t0, torch.distributed.ReduceOp.MAX if world > 1 else None)
+    barrier()
+
+    value = total_audio / (max_ms / 1e3)
+    avg_len = 4 + total_tokens / len(clips) / 2
+    dec_bytes = decode_bytes_per_token(dims, int(avg_len))
+    line = {
+        'metric': 'whole-box stream throughput (BASELINE config 4)', 'value': round(value, 2), 'unit': 'audio-s/s',
+        'n_gpus': world, 'steps': 1, 'warmup': args.warmup, 'ms_per_step': round(max_ms, 3),
+        'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f16', 'data': 'synthetic',
+        'config': {'workload': f'BASELINE config 4: {len(clips)} clips (audio seeds 0..{len(clips) - 1}, U[5,30] s '
+                               f'lengths from default_rng(0), padded to 30 s), round(7.5 tokens/s x s) forced tokens; '
+                               'static longest-first partition over ranks; one step = the whole set',
+                   'model': 'whisper-large-v3-turbo architecture, random-init seed 0 (fp16)', 'clips': len(clips),
+                   'audio_seconds': round(total_audio, 2), 'tokens': total_tokens,
+                   'parallelism': f'replicas{world}' if world > 1 else 'single',
+                   'l2': 'working set larger than L2 (347 MB per decode step, 1.26 GB encoder weights)'},
+        'e2e': {'value': round(total_audio / e2e_s, 2), 'unit': 'audio-s/s',
+                'h2d_bytes_per_step': len(clips) * 480000 * 4, 'd2h_bytes_per_step': total_tokens * 8},
+        'rank0_clips': len(mine),
+        'roofline_decode_step': {'bound': 'hbm', 'bytes_per_token': dec_bytes,
+                                 'note': 'per-token decode bytes at the mean self-attention length'},
+        'gpu_launches': int(launches),
+        'clocks': clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu_model, cpu_audio = cpu_reference_sample()
+            _, t = run_cpu_sample(cpu_model, cpu_audio, 8)
+            per_tok = t['decode_s'] / max(1, t['n_tokens'])
+            cpu_s = len(clips) * (t['mel_s'] + t['encoder_s']) + total_tokens * per_tok
+            line['cpu_baseline'] = {
+                'value': round(total_audio / cpu_s, 3), 'unit': 'audio-s/s', 'cores': torch.get_num_threads(),
+                'kind': 'port', 'sample': 'CPU fp32 log-mel + encoder of one 30 s clip + 8 decode steps (oracle/hf_cpu.py), '
+                                          'extrapolated to the 256 clips and their forced tokens'}
+        except Exception as exc:  # the baseline is reported, never required
+            line['cpu_baseline'] = {'value': None, 'unit': 'audio-s/s', 'error': f'{type(exc).__name__}: {exc}'}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument('--gpus', type=int, default=1)
@@ -322,6 +450,7 @@ def main():
     parser.add_argument('--warmup', type=int, default=3)
     parser.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     parser.add_argument('--no-cpu-baseline', action='store_true')
+    parser.add_argument('--workload', choices=('clip30', 'clips256'), default='clip30')
     args = parser.parse_args()
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
@@ -334,6 +463,8 @@ def main():
         torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=600),
                                              device_id=torch.device('cuda', local_rank))
     try:
+        if args.workload == 'clips256':
+            return bench_clips(args, rank, world, local_rank)
         return bench_ours(args, rank, world, local_rank)
     finally:
         if world > 1:

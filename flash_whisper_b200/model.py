@@ -256,13 +256,20 @@ class CustomModel:
         host[audio.size:] = 0.0
         self.wave.copy_(self.wave_host, non_blocking=True)
 
+    def run_steps(self, n):
+        """n decode steps: whole CHUNK-step graphs, then the remainder launched directly."""
+        for _ in range(n // self.chunk):
+            self.run_chunk()
+        if n % self.chunk:
+            self.ext.decoder_step(self.dec_desc, n % self.chunk)
+
     @torch.inference_mode()
     def decode_device(self, n_tokens):
-        """Device-resident pipeline after the waveform is in self.wave: front, prompt, chunks."""
+        """Device-resident pipeline after the waveform is in self.wave: front, prompt (which yields
+        the first token) and exactly n_tokens - 1 further decode steps."""
         self.run_front()
         self.run_prompt()
-        for _ in range(-(-(n_tokens - 1) // self.chunk)):
-            self.run_chunk()
+        self.run_steps(max(0, n_tokens - 1))
 
     # ---- public API --------------------------------------------------------------------------
     @torch.inference_mode()
@@ -290,8 +297,7 @@ class CustomModel:
         n_chunks = -(-(limit - 1) // self.chunk) if limit > 1 else 0
         token_ids = []
         if not stop_at_eos:
-            for _ in range(n_chunks):
-                self.run_chunk()
+            self.run_steps(max(0, limit - 1))
             self.tokens_host[:limit].copy_(self.tokens[:limit], non_blocking=True)
             ev[3].synchronize()
             ttft = time.perf_counter() - start
