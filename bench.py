@@ -146,6 +146,11 @@ def decode_bytes_per_token(dims, length):
     return L * per_layer + cross + self_kv + lm + emb
 
 
+def host_threads():
+    """All host cores this process may use (torchrun sets OMP_NUM_THREADS=1 for its ranks)."""
+    return len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else (os.cpu_count() or 1)
+
+
 def cpu_reference_sample(n_tokens=8, threads=None):
     """CPU fp32 reference path on a bounded sample: full mel + encoder + n_tokens decode steps.
 
@@ -173,7 +178,7 @@ def run_cpu_sample(model, audio, n_tokens):
 def bench_reference(args, rank, world):
     if rank != 0:
         return 0
-    threads = torch.get_num_threads()
+    threads = host_threads()
     model, audio = cpu_reference_sample(threads=threads)
     n_sample = 8
     for _ in range(max(0, min(args.warmup, 1))):
@@ -332,7 +337,7 @@ def bench_ours(args, rank, world, local_rank):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu_model, cpu_audio = cpu_reference_sample()
+            cpu_model, cpu_audio = cpu_reference_sample(threads=host_threads())
             v, t = run_cpu_sample(cpu_model, cpu_audio, 8)
             line['cpu_baseline'] = {
                 'value': round(v, 3), 'unit': 'ms', 'cores': torch.get_num_threads(), 'kind': 'port',
@@ -428,7 +433,7 @@ def bench_clips(args, rank, world, local_rank):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu_model, cpu_audio = cpu_reference_sample()
+            cpu_model, cpu_audio = cpu_reference_sample(threads=host_threads())
             _, t = run_cpu_sample(cpu_model, cpu_audio, 8)
             per_tok = t['decode_s'] / max(1, t['n_tokens'])
             cpu_s = len(clips) * (t['mel_s'] + t['encoder_s']) + total_tokens * per_tok
