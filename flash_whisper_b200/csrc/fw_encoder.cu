@@ -7,7 +7,7 @@
 //
 //  * gemm_tc_kernel: C[128 x BN] tile per CTA. Warp 0 issues TMA loads (128B-swizzled K-major
 //    tiles) into a STAGES-deep shared-memory ring, warp 1 allocates TMEM and issues
-//    tcgen05.mma (M=128, N=BN, K=16, fp16 in / fp32 accumulate in TMEM), warps 2-5 read the
+//    tcgen05.mma (M=128, N=BN, K=16, fp16 in / fp32 accumulate in TMEM), warps 2-9 read the
 //    accumulator back with tcgen05.ld and run the fused epilogue (bias, GELU, residual add,
 //    positions, q scaling, cross-K/V scatter). Weight tiles of the first stages are requested
 //    before the PDL wait.
@@ -127,12 +127,17 @@ struct GemmEpi {
   int vt_col;  // FW_EPI_QKV_VT: first column written transposed into R
 };
 
-__device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int n, const uint32_t (&r)[16]) {
+__device__ __forceinline__ bool epi_reads_r(int mode) { return mode == FW_EPI_BIAS_RESID || mode == FW_EPI_GELU_POS; }
+
+// One row's 16 columns n..n+15: accumulator bits r, bias from the tile's shared-memory copy sb (8
+// halves per uint4, null when the GEMM has none), residual R[row, n..n+15] in ra | rb when the mode
+// reads R.
+__device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int n, const uint32_t (&r)[16],
+                                                 const uint4* sb, const uint4& ra, const uint4& rb) {
   float o[16];
   float bias[16];
-  if (ep.bias) {
-    const uint4* b4 = reinterpret_cast<const uint4*>(ep.bias + n);
-    const uint4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+  if (sb != nullptr) {
+    const uint4 b0 = sb[0], b1 = sb[1];
     const half* bh0 = reinterpret_cast<const half*>(&b0);
     const half* bh1 = reinterpret_cast<const half*>(&b1);
 #pragma unroll
@@ -162,11 +167,9 @@ __device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int
   if (ep.mode == FW_EPI_BIAS_GELU) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j] = gelu_erf(o[j]);
-  } else if (ep.mode == FW_EPI_BIAS_RESID || ep.mode == FW_EPI_GELU_POS) {
-    const uint4* r4 = reinterpret_cast<const uint4*>(ep.R + static_cast<size_t>(row) * ep.ldr + n);
-    const uint4 a0 = r4[0], a1 = r4[1];
-    const half* rh0 = reinterpret_cast<const half*>(&a0);
-    const half* rh1 = reinterpret_cast<const half*>(&a1);
+  } else if (epi_reads_r(ep.mode)) {
+    const half* rh0 = reinterpret_cast<const half*>(&ra);
+    const half* rh1 = reinterpret_cast<const half*>(&rb);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const float res = __half2float(j < 8 ? rh0[j] : rh1[j - 8]);
@@ -193,10 +196,13 @@ __device__ __forceinline__ void epilogue_store16(const GemmEpi& ep, int row, int
 // order (tile t covers m tile t % m_tiles and n tile t / m_tiles), so the CTAs that run together
 // share weight (B) slices. Warp 0 streams A and B k-blocks through a STAGES-deep ring (the B
 // tiles of the first stages are requested before the PDL wait), warp 1 issues the MMAs into one of
-// kAccBufs TMEM accumulators, warps 2-5 drain the previous accumulator through the epilogue while
+// kAccBufs TMEM accumulators, warps 2-9 drain the previous accumulator through the epilogue while
 // the next tile's MMAs run. BN = kSub * kSubN columns per tile: kSub MMAs of N = kSubN per K step.
+constexpr int kGemmEpiWarps = 8;  // two per TMEM lane quadrant, each draining half of the columns
+constexpr int kGemmThreads = 32 * (2 + kGemmEpiWarps);
+
 template <int kSubN, int kSub, int STAGES, bool kConv>
-__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB, int num_kb,
                                                          int conv_c, int conv_stride, GemmEpi ep, int m_tiles,
                                                          int n_tiles, const char* l2_next, unsigned l2_bytes) {
@@ -215,6 +221,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   __shared__ __align__(8) uint64_t acc_full[kAccBufs];
   __shared__ __align__(8) uint64_t acc_empty[kAccBufs];
   __shared__ uint32_t tmem_base_sh;
+  __shared__ __align__(16) uint4 s_bias[2][BN / 8];
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -231,7 +238,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     }
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kGemmEpiWarps);
     }
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
@@ -338,26 +345,63 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       }
     }
   } else {
+    // Epilogue warps 2..9: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows) and the 32-column
+    // chunks c with (c / 32) % 2 == (w - 2) / 4. What does not depend on the accumulator is fetched
+    // while the tile's MMAs run: the tile's bias slice into shared memory (double-buffered by tile,
+    // one named barrier of the epilogue threads per tile) and this row's residual for the first
+    // chunk; the residual of the next chunk is loaded while the current one is processed.
     pdl_wait();
-    const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to this warp
+    const int q = warp & 3;
+    const int half_id = (warp - 2) >> 2;
+    const int et = threadIdx.x - 64;
+    const bool reads_r = epi_reads_r(ep.mode);
+    bool failed = false;
     int local = 0;
     for (int t = first; t < tiles; t += gridDim.x, ++local) {
       const int buf = local % kAccBufs;
       const uint32_t use = local / kAccBufs;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
       const int row = m0 + q * 32 + lane;
-      if (!mbar_wait_warp(&acc_full[buf], use & 1u)) {
-        enc_flag(FW_DEVERR_TIMEOUT);
-        break;
+      const bool row_ok = row < ep.M;
+      uint4* sb = s_bias[local & 1];
+      if (ep.bias != nullptr) {
+        const uint4* b4 = reinterpret_cast<const uint4*>(ep.bias + n0);
+        for (int i = et; i < BN / 8; i += 32 * kGemmEpiWarps) sb[i] = __ldg(b4 + i);
+      }
+      const uint4* r4 = reinterpret_cast<const uint4*>(ep.R + (row_ok ? static_cast<size_t>(row) * ep.ldr : 0) + n0);
+      const bool load_r = reads_r && row_ok;
+      uint4 cur[4] = {}, nxt[4] = {};
+      if (load_r) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) cur[i] = r4[half_id * 4 + i];
+      }
+      // Every epilogue warp reaches this barrier once per tile, also after a timed-out wait (it then
+      // skips the tile), so no warp can be left waiting here.
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kGemmEpiWarps) : "memory");  // bias slice visible
+      const uint4* sbias = ep.bias != nullptr ? sb : nullptr;
+      if (failed || !mbar_wait_warp(&acc_full[buf], use & 1u)) {
+        if (!failed) enc_flag(FW_DEVERR_TIMEOUT);
+        failed = true;
+        continue;
       }
       tc_fence_after();
       const uint32_t d = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
-        tc_ld16(d + static_cast<uint32_t>(c), r);
+      for (int c = half_id * 32; c < BN; c += 64) {
+        uint32_t r0[16], r1[16];
+        tc_ld16(d + static_cast<uint32_t>(c), r0);
+        tc_ld16(d + static_cast<uint32_t>(c + 16), r1);
+        if (load_r && c + 64 < BN) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) nxt[i] = r4[(c + 64) / 8 + i];
+        }
         tc_wait_ld();
-        if (row < ep.M) epilogue_store16(ep, row, n0 + c, r);
+        if (row_ok) {
+          epilogue_store16(ep, row, n0 + c, r0, sbias ? sbias + c / 8 : nullptr, cur[0], cur[1]);
+          epilogue_store16(ep, row, n0 + c + 16, r1, sbias ? sbias + c / 8 + 2 : nullptr, cur[2], cur[3]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) cur[i] = nxt[i];
       }
       tc_fence_before();
       __syncwarp();
@@ -763,7 +807,7 @@ static int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int K, in
     const int m_tiles = (ep.M + 127) / 128, n_tiles = ep.N / BN;
     const int tiles = m_tiles * n_tiles;
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    e = launch(kern, dim3(grid), dim3(192), smem, s, pdl, ta, tb, K / 64, conv_c, conv_stride, ep, m_tiles, n_tiles,
+    e = launch(kern, dim3(grid), dim3(kGemmThreads), smem, s, pdl, ta, tb, K / 64, conv_c, conv_stride, ep, m_tiles, n_tiles,
                static_cast<const char*>(l2_next), static_cast<unsigned>(l2_bytes));
   }
   return launch_status(e, "gemm_tc");
