@@ -46,10 +46,9 @@ N_TOKENS = 224
 N_CLIPS = 256
 TOKENS_PER_SECOND = 7.5
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
-# dram__bytes_read.sum + dram__bytes_write.sum of one lm_head_kernel launch (ncu --set full, see
-# profiles/lm_head_argmax_decode_step.txt): 132.92 MB read + 6.13 MB written (evicted dirty L2 lines
-# of earlier kernels; the kernel itself writes 8 bytes).
-LM_HEAD_TRAFFIC_BYTES = 132_922_368 + 6_128_640
+# dram__bytes_read.sum + dram__bytes_write.sum of one lm_head_q_kernel launch from an ncu capture of
+# the decode step (profiles/lm_head_q_decode_step.txt); None until captured.
+LM_HEAD_TRAFFIC_BYTES = None
 
 
 def peaks():
@@ -135,13 +134,15 @@ def partition(clips, world):
     return parts
 
 
-def decode_bytes_per_token(dims, length):
-    """Algorithmic HBM bytes of one decode step at self-attention length `length`."""
+def decode_bytes_per_token(dims, length, lm_pruned=True):
+    """Algorithmic HBM bytes of one decode step at self-attention length `length`. With the pruned
+    LM head the vocab matrix is read as int8 plus 16 bytes of scale and bounds per row (the fp16
+    rows rescored exactly, about 8 per 351-row block on these weights, are left out)."""
     d, f, L = dims.d_model, dims.ffn, dims.decoder_layers
     per_layer = 2 * (3 * d * d + 3 * d + 3 * d * d + 3 * d + 2 * f * d + f + d + 6 * d)  # weights + biases + LN
     cross = L * 2 * dims.heads * dims.enc_len * dims.head_dim * 2
     self_kv = L * 2 * dims.heads * length * dims.head_dim * 2
-    lm = dims.vocab * d * 2 + dims.vocab * 1 + 2 * d * 2
+    lm = (dims.vocab * (d + 16) if lm_pruned else dims.vocab * d * 2) + dims.vocab * 1 + 2 * d * 2
     emb = 2 * d * 2
     return L * per_layer + cross + self_kv + lm + emb
 
@@ -275,17 +276,26 @@ def bench_ours(args, rank, world, local_rank):
         dec_ms += ev[3].elapsed_time(ev[4]) / reps
     us_per_token = maxed(dec_ms * 1e3 / dec_steps)
 
-    # (3) LM-head kernel alone (the largest single kernel of the decode step), same stream
+    # (3) LM-head kernel alone (the largest single kernel of the decode step), same stream, on the
+    # final-LayerNorm output of the last decoded step (the stand-alone entry takes x after the LN)
     lm_iters = 50
     ext = model.ext
     best = torch.zeros(1, dtype=torch.long, device='cuda')
+    x_lm = torch.nn.functional.layer_norm(model.h.float(), (dims.d_model,), model.dec.final_ln[0].float(),
+                                          model.dec.final_ln[1].float(), dims.eps).half()
+
+    def lm_once():
+        if model.lm_q is not None:
+            ext.lm_head_argmax_q(x_lm, model.dec.lm_head, model.lm_q, model.lm_rp, model.base_mask, best)
+        else:
+            ext.lm_head_argmax(x_lm, model.dec.lm_head, model.base_mask, best)
     for _ in range(3):
-        ext.lm_head_argmax(model.h, model.dec.lm_head, model.base_mask, best)
+        lm_once()
         best.zero_()
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(lm_iters):
-        ext.lm_head_argmax(model.h, model.dec.lm_head, model.base_mask, best)
+        lm_once()
     e1.record(stream)
     torch.cuda.synchronize()
     lm_us = e0.elapsed_time(e1) * 1e3 / lm_iters
@@ -304,8 +314,10 @@ def bench_ours(args, rank, world, local_rank):
 
     pk = peaks()
     avg_len = 4 + N_TOKENS / 2
-    step_bytes = decode_bytes_per_token(dims, int(avg_len))
-    lm_bytes = dims.vocab * dims.d_model * 2 + dims.vocab + dims.d_model * 2
+    pruned = model.lm_q is not None
+    step_bytes = decode_bytes_per_token(dims, int(avg_len), pruned)
+    lm_bytes = (dims.vocab * (dims.d_model + 16) if pruned else dims.vocab * dims.d_model * 2) + dims.vocab + \
+        dims.d_model * 2
     lm_gbs = lm_bytes / (lm_us * 1e-6) / 1e9
     dec_gbs = step_bytes / (us_per_token * 1e-6) / 1e9
     # our kernels per step: log-mel 2; encoder: 2 convs, 7 per layer, final LN, cross-K/V GEMM;
@@ -325,7 +337,9 @@ def bench_ours(args, rank, world, local_rank):
         'decode_us_per_token': round(us_per_token, 3),
         'stages_ms': {'mel': round(mel_ms, 4), 'encoder': round(enc_ms, 4), 'decode': round(dec_ms, 4)},
         'throughput_audio_s_per_s': round(world * SECONDS / (step_ms / 1e3), 2),
-        'roofline': {'bound': 'hbm', 'kernel': 'lm_head_argmax (GEMV 51866x1280 + argmax)',
+        'roofline': {'bound': 'hbm', 'kernel': ('lm_head_q (int8 GEMV 51866x1280 with per-row bounds, exact fp16 '
+                                                'rescoring of the rows that can win, argmax)' if pruned else
+                                                'lm_head_argmax (GEMV 51866x1280 + argmax)'),
                      'achieved': round(lm_gbs, 1), 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
                      'frac': round(lm_gbs / pk['hbm_gbs'], 4), 'traffic': LM_HEAD_TRAFFIC_BYTES, 'peak_source': pk['source'],
                      'launch_us': round(lm_us, 3), 'bytes_per_launch': lm_bytes},

@@ -39,6 +39,7 @@ class Decoder(ctypes.Structure):
         ('h', vp), ('qkv', vp), ('attn', vp), ('cq', vp), ('ffn', vp),
         ('part_m', vp), ('part_l', vp), ('part_acc', vp), ('ws_splits', c_int64),
         ('counters', vp), ('cur', vp), ('state', vp), ('tokens', vp), ('best', vp), ('n_tokens', c_int64),
+        ('lm_q', vp), ('lm_rp', vp),
     ]
 
 
@@ -69,6 +70,8 @@ _SIGNATURES = {
                                     c_float, vp]),
     'fw_decode_attention_noalloc': (c_int, [vp, vp, vp, vp, vp, vp, vp, c_int, c_int, c_float, vp]),
     'fw_lm_head_argmax': (c_int, [vp, vp, vp, c_int, c_int, vp, vp]),
+    'fw_lm_quantize': (c_int, [vp, c_int, c_int, vp, vp, vp]),
+    'fw_lm_head_argmax_q': (c_int, [vp, vp, vp, vp, vp, c_int, c_int, vp, vp]),
     'fw_argmax_finalize': (c_int, [vp, vp, c_int64, vp, vp, c_int, vp]),
     'fw_embed_pos': (c_int, [vp, vp, vp, vp, vp, c_int, c_int, c_int, c_int, vp]),
     'fw_gelu': (c_int, [vp, vp, c_int64, vp]),

@@ -854,6 +854,8 @@ struct LmParams {
   const half* beta;
   float eps;
   const half* w;
+  const int8_t* wq;   // lm_head_q_kernel: int8 rows and per-row {scale, a, c2, 0} (fw_lm_quantize)
+  const float4* rp;
   int vocab;
   int rows_per_cta;
   const bool* mask;
@@ -1001,6 +1003,451 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
         *p.counter = 0u;
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Pruned LM head: the same argmax as lm_head_kernel, reading half the bytes.
+//
+// fw_lm_quantize stores each vocab row w_r as int8 q_r with a per-row scale s_r (s_r = max|w_r| /
+// 127) and two per-row error terms, computed exactly in fp64 and rounded up to fp32:
+//   a_r  = max_i |w_ri - s_r q_ri| + 1e-5 max_i |w_ri|
+//   c2_r = 0.51 s_r sum_i |q_ri|
+// The kernel quantises the LayerNorm output x to 14-bit integers xq (scale sx = max|x| / 8191, so
+// |x_i - sx xq_i| <= 0.51 sx), streams q, and forms the exact integer S_r = sum_i xq_i q_ri with
+// dp2a. approx_r = s_r sx S_r then satisfies |dot_r - approx_r| <= B_r with
+//   B_r = (|x|_1 a_r + sx c2_r + 4e-7 |approx_r|) (1 + 1e-5),
+// where dot_r is the fp32 value the exact kernel computes (its own rounding error is at most
+// 45 * 2^-24 |x|_1 max|w_r|, inside the 1e-5 term; the other terms bound the two quantisations
+// and the fp32 rounding of approx_r). With L_r = approx_r - B_r, U_r = approx_r + B_r and
+// T = max over this CTA's unsuppressed rows of L_r, a row with U_r < T - m, m = 2^-9 (|T| + 2 max
+// B) + 2^-23, has fp16(dot_r) strictly below fp16(dot) of the row that set T (the margin exceeds
+// the fp16 spacing at those magnitudes), so it can neither win nor tie. The CTA recomputes the
+// remaining rows exactly with dot1280 (the arithmetic of lm_head_kernel, bit for bit) and takes
+// the packed-key maximum of those; the global argmax row is always among its CTA's survivors, so
+// the result equals lm_head_kernel's. If T is not finite or |T| >= 32768 (fp16 overflow makes
+// distant values tie at infinity) every unsuppressed row of the CTA is recomputed.
+constexpr int kQStages = 8;                             // TMA ring depth (16 KB stages)
+constexpr int kQTileRows = 128;                         // MMA M: vocab rows per accumulator tile
+constexpr int kQBoxRows = 32;                           // rows per TMA box
+constexpr int kQChunk = 128;                            // K bytes per stage (one 128-byte swizzle row)
+constexpr int kQChunks = kHidden / kQChunk;             // 10 stages per tile
+constexpr int kQStageBytes = kQTileRows * kQChunk;      // 16 KB
+constexpr int kQXBytes = kQChunks * 8 * kQChunk;        // B operand: 8 rows (x_hi, x_lo, 0...) x 1280
+constexpr int kQSmem = kQStages * kQStageBytes + kQXBytes + 1024;
+constexpr float kXqMax = 8191.f;
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// kind::i8 instruction descriptor: D s32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1),
+// both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t make_idesc_s8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+__device__ __forceinline__ void tc_ld2(uint32_t taddr, uint32_t& a, uint32_t& b) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
+// Exact fp32 dot of kRows fp16 rows at arbitrary addresses with x: per row the arithmetic of
+// dot1280_rows (lane order, fma chain, butterfly), so the results are bit-identical to it.
+template <int kRows>
+__device__ __forceinline__ void dot1280_ptrs(const half* const (&rows)[kRows], const float (&xf)[40],
+                                             float (&out)[kRows]) {
+  const int lane = threadIdx.x & 31;
+  float acc[kRows];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+  uint4 wv[kRows][5];
+#pragma unroll
+  for (int c = 0; c < 5; ++c)
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) wv[r][c] = __ldg(reinterpret_cast<const uint4*>(rows[r]) + lane + 32 * c);
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const half2* p = reinterpret_cast<const half2*>(&wv[r][c]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(p[k]);
+        acc[r] = fmaf(f.x, xf[c * 8 + 2 * k], acc[r]);
+        acc[r] = fmaf(f.y, xf[c * 8 + 2 * k + 1], acc[r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) out[r] = acc[r];
+}
+
+// Warp roles: warp 0 streams the CTA's int8 rows (32-row x 128-byte TMA boxes, 128B swizzle) through
+// a kQStages ring, the first stages requested before the PDL wait; warp 1 owns TMEM and issues
+// tcgen05.mma kind::i8 (M = 128 rows, N = 8, K = 32) of each tile against the B operand
+// [x_hi; x_lo; 0 ...] (xq = 128 x_hi + x_lo, both int8) into one of two TMEM accumulators; warps 2-5
+// read each row's two int32 sums (tcgen05.ld, TMEM lane = row) and form approx_r and B_r; all
+// eight warps then select and rescore the surviving rows.
+template <bool kLN, bool kFinalize>
+__global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant__ CUtensorMap tmW, LmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[kQStages];
+  __shared__ __align__(8) uint64_t empty[kQStages];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ float red[16];
+  __shared__ __align__(16) half ys[kHidden];
+  __shared__ __align__(16) float4 rps[kLmMaxRowsPerCta];
+  __shared__ float ub[kLmMaxRowsPerCta];
+  __shared__ unsigned short cand[kLmMaxRowsPerCta];
+  __shared__ uint8_t msk[2][kLmMaxRowsPerCta];
+  __shared__ float warp_l[8], warp_b[8], xstat[2][8];
+  __shared__ unsigned long long warp_best[8];
+  __shared__ int ncand;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* stages = smem_raw + (base - raw);
+  uint8_t* xb = stages + kQStages * kQStageBytes;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r0 = blockIdx.x * p.rows_per_cta;
+  const int r1 = min(p.vocab, r0 + p.rows_per_cta);
+  const int nrows = max(0, r1 - r0);
+  const int n_tiles = (nrows + kQTileRows - 1) / kQTileRows;
+  const int total = n_tiles * kQChunks;
+  auto issue = [&](int it, uint64_t policy) {
+    const int t = it / kQChunks, c = it - t * kQChunks, s = it % kQStages;
+    const int boxes = (min(kQTileRows, nrows - t * kQTileRows) + kQBoxRows - 1) / kQBoxRows;
+    mbar_arrive_expect_tx(&full[s], static_cast<unsigned>(boxes * kQBoxRows * kQChunk));
+    for (int b = 0; b < boxes; ++b)
+      tma_load_2d_hint(stages + s * kQStageBytes + b * kQBoxRows * kQChunk, &tmW, &full[s], c * kQChunk,
+                       r0 + t * kQTileRows + b * kQBoxRows, policy);
+  };
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < kQStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_fence_init();
+    tma_prefetch_desc(&tmW);
+    const uint64_t policy = policy_evict_first();
+    for (int it = 0; it < kQStages && it < total; ++it) issue(it, policy);  // weights: before the wait
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, 32);
+    tmem_relinquish();
+  }
+  // Constant per-row data (suppress flags, scales and bounds) and the zero rows of B.
+  for (int i = threadIdx.x; i < nrows; i += 256) {
+    msk[0][i] = p.mask ? static_cast<uint8_t>(p.mask[r0 + i]) : 0;
+    msk[1][i] = p.first_mask ? static_cast<uint8_t>(p.first_mask[r0 + i]) : 0;
+    rps[i] = p.rp[r0 + i];
+  }
+  for (int i = threadIdx.x; i < kQXBytes / 16; i += 256) reinterpret_cast<uint4*>(xb)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) ncand = 0;
+  float g[5], be[5];
+  if (kLN) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      g[i] = __half2float(p.gamma[threadIdx.x + i * 256]);
+      be[i] = __half2float(p.beta[threadIdx.x + i * 256]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  pdl_wait();
+  pdl_trigger();
+
+  float xv[5];
+  if (kLN) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) xv[i] = __half2float(p.h[threadIdx.x + i * 256]);
+    float mean, inv;
+    ln1280_stats(xv, red, p.eps, mean, inv);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const half y = __float2half(ln_apply(xv[i], mean, inv, g[i], be[i]));
+      ys[threadIdx.x + i * 256] = y;
+      xv[i] = __half2float(y);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const half y = p.h[threadIdx.x + i * 256];
+      ys[threadIdx.x + i * 256] = y;
+      xv[i] = __half2float(y);
+    }
+  }
+  // max|x| and |x|_1 of the fp16 LayerNorm output
+  {
+    float mx = 0.f, sm = 0.f;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      mx = fmaxf(mx, fabsf(xv[i]));
+      sm += fabsf(xv[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    }
+    if (lane == 0) {
+      xstat[0][warp] = mx;
+      xstat[1][warp] = sm;
+    }
+  }
+  __syncthreads();
+  float xmax = 0.f, nx1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    xmax = fmaxf(xmax, xstat[0][i]);
+    nx1 += xstat[1][i];
+  }
+  nx1 *= 1.0001f;  // covers the fp32 rounding of the sum
+  const float sx = xmax > 0.f ? xmax / kXqMax : 0.f;
+  const float xinv = xmax > 0.f ? kXqMax / xmax : 0.f;
+  // B operand: row 0 = x_hi, row 1 = x_lo of xq = rint(x / sx) (|xq| <= 8191), one 8-row
+  // 128B-swizzled atom per 128-element K chunk (16-byte unit j of row n stored at unit j ^ n).
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const int k = threadIdx.x + i * 256;
+    const int xq = max(-8191, min(8191, __float2int_rn(xv[i] * xinv)));
+    const int xh = (xq + 64) >> 7;  // floor((xq + 64) / 128), in [-64, 64]
+    const int xl = xq - (xh << 7);  // in [-64, 63]
+    const int c = k >> 7, kk = k & 127;
+    uint8_t* atom = xb + c * 8 * kQChunk;
+    atom[0 * kQChunk + ((((kk >> 4) ^ 0) & 7) << 4) + (kk & 15)] = static_cast<uint8_t>(static_cast<int8_t>(xh));
+    atom[1 * kQChunk + ((((kk >> 4) ^ 1) & 7) << 4) + (kk & 15)] = static_cast<uint8_t>(static_cast<int8_t>(xl));
+  }
+  fence_proxy_async_shared();  // B written by the generic proxy, read by the tensor core
+  __syncthreads();
+  float xf[40];
+  load_x40(ys, xf);
+
+  const uint8_t* mask = msk[0];
+  if (kFinalize && p.first_mask && p.prompt_len > 0 && p.state[0] == p.prompt_len - 1) mask = msk[1];
+
+  // ---- pass 1: int8 tensor-core GEMV, bounds per row ----
+  float lmax = -INFINITY, bmax = 0.f;
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t policy = policy_evict_first();
+      for (int it = kQStages; it < total; ++it) {
+        const int s = it % kQStages;
+        if (!mbar_wait(&empty[s], ((it / kQStages) & 1) ^ 1)) {
+          flag_error(FW_DEVERR_TIMEOUT);
+          break;
+        }
+        issue(it, policy);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_s8(kQTileRows, 8);
+      const uint32_t xaddr = smem_u32(xb);
+      bool ok = true;
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        const int buf = t & 1;
+        if (t >= 2 && !mbar_wait(&acc_empty[buf], ((t >> 1) - 1) & 1)) {
+          flag_error(FW_DEVERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * 8);
+        for (int c = 0; c < kQChunks; ++c) {
+          const int it = t * kQChunks + c, s = it % kQStages;
+          if (!mbar_wait(&full[s], (it / kQStages) & 1)) {
+            flag_error(FW_DEVERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sw128_desc(base + s * kQStageBytes);
+          const uint64_t bdesc = sw128_desc(xaddr + c * 8 * kQChunk);
+#pragma unroll
+          for (int kk = 0; kk < kQChunk / 32; ++kk)
+            tc_mma_i8(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&acc_full[buf]);
+      }
+    }
+  } else if (warp < 6) {
+    const int q = warp & 3;  // TMEM lanes 32q..32q+31 = tile rows 32q..32q+31
+    for (int t = 0; t < n_tiles; ++t) {
+      const int buf = t & 1;
+      if (!mbar_wait_warp(&acc_full[buf], (t >> 1) & 1)) {
+        flag_error(FW_DEVERR_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+      uint32_t v0, v1;
+      tc_ld2(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 8), v0, v1);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      const int li = t * kQTileRows + q * 32 + lane;
+      if (li < nrows) {
+        const int sum = 128 * static_cast<int>(v0) + static_cast<int>(v1);  // sum_i q_ri xq_i, exact
+        const float4 prm = rps[li];
+        const float approx = prm.x * sx * static_cast<float>(sum);
+        const float b = (nx1 * prm.y + sx * prm.z + 4e-7f * fabsf(approx)) * 1.00001f + 1e-30f;
+        if (mask[li]) {
+          ub[li] = -INFINITY;
+        } else {
+          ub[li] = approx + b;
+          lmax = fmaxf(lmax, approx - b);
+          bmax = fmaxf(bmax, b);
+          if (!isfinite(approx) || !isfinite(b)) bmax = INFINITY;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+  }
+  if (lane == 0) {
+    warp_l[warp] = lmax;
+    warp_b[warp] = bmax;
+  }
+  __syncthreads();
+
+  // ---- row selection: U_r >= T - m (every row when the bound is unusable) ----
+  float t = -INFINITY, bm = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    t = fmaxf(t, warp_l[i]);
+    bm = fmaxf(bm, warp_b[i]);
+  }
+  const bool all_rows = !(fabsf(t) < 32768.f) || !(bm < 32768.f);
+  const float thr = t - (0x1p-9f * (fabsf(t) + 2.f * bm) + 0x1p-23f);
+  for (int i = threadIdx.x; i < nrows; i += 256) {
+    if (!mask[i] && (all_rows || ub[i] >= thr)) cand[atomicAdd(&ncand, 1)] = static_cast<unsigned short>(i);
+  }
+  __syncthreads();
+
+  // ---- pass 2: exact fp16 logits of the surviving rows, two rows per warp at a time ----
+  const int nc = ncand;
+  unsigned long long mine = 0;
+  for (int j = 2 * warp; j < nc; j += 16) {
+    const int ra = r0 + cand[j];
+    const int rb = j + 1 < nc ? r0 + cand[j + 1] : ra;
+    const half* rows[2] = {p.w + static_cast<size_t>(ra) * kHidden, p.w + static_cast<size_t>(rb) * kHidden};
+    float acc[2];
+    dot1280_ptrs<2>(rows, xf, acc);
+    const unsigned long long ka = pack_score(round_half(acc[0]), ra);
+    const unsigned long long kb = pack_score(round_half(acc[1]), rb);
+    mine = ka > mine ? ka : mine;
+    mine = kb > mine ? kb : mine;
+  }
+  if (lane == 0) warp_best[warp] = mine;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+  if (threadIdx.x == 0) {
+    unsigned long long m = 0;
+    for (int i = 0; i < 8; ++i) m = warp_best[i] > m ? warp_best[i] : m;
+    if (m) atomicMax(p.best, m);
+    if (kFinalize) {
+      __threadfence();
+      const unsigned prev = atomicAdd(p.counter, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence();
+        const unsigned long long b = atomicExch(p.best, 0ull);
+        finalize_token(b, p.tokens, p.n_tokens, p.state, p.cur, p.max_pos, p.prompt_len);
+        *p.counter = 0u;
+      }
+    }
+  }
+}
+
+// One warp per vocab row: int8 row, scale and the two error terms of lm_head_q_kernel.
+__global__ void __launch_bounds__(256) lm_quantize_kernel(const half* __restrict__ w, int vocab,
+                                                          int8_t* __restrict__ wq, float4* __restrict__ rp) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= vocab) return;
+  const half* wr = w + static_cast<size_t>(row) * kHidden;
+  float v[40];
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+    const uint4 u = reinterpret_cast<const uint4*>(wr)[lane + 32 * c];
+    const half2* h2 = reinterpret_cast<const half2*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(h2[k]);
+      v[8 * c + 2 * k] = f.x;
+      v[8 * c + 2 * k + 1] = f.y;
+    }
+  }
+  float wmax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 40; ++i) wmax = fmaxf(wmax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+  const float s = wmax > 0.f ? wmax / 127.f : 1.f;
+  double err = 0.0;
+  int q1 = 0;
+  int8_t q[40];
+#pragma unroll
+  for (int i = 0; i < 40; ++i) {
+    const int qi = max(-127, min(127, __float2int_rn(v[i] / s)));
+    q[i] = static_cast<int8_t>(qi);
+    q1 += abs(qi);
+    err = fmax(err, fabs(static_cast<double>(v[i]) - static_cast<double>(qi) * static_cast<double>(s)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    err = fmax(err, __shfl_xor_sync(0xffffffffu, err, o));
+    q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+  }
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+    uint2 packed;
+    packed.x = (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 0]))) |
+               (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 1])) << 8) |
+               (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 2])) << 16) |
+               (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 3])) << 24);
+    packed.y = (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 4]))) |
+               (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 5])) << 8) |
+               (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 6])) << 16) |
+               (static_cast<uint32_t>(static_cast<uint8_t>(q[8 * c + 7])) << 24);
+    reinterpret_cast<uint2*>(wq + static_cast<size_t>(row) * kHidden)[lane + 32 * c] = packed;
+  }
+  if (lane == 0) {
+    const double a = err + 1e-5 * static_cast<double>(wmax);
+    const double c2 = 0.51 * static_cast<double>(s) * static_cast<double>(q1);
+    rp[row] = make_float4(s, __double2float_ru(a), __double2float_ru(c2), 0.f);
   }
 }
 
@@ -1363,6 +1810,37 @@ static int launch_lm_head(LmParams p, cudaStream_t s, bool pdl) {
   return launch_status(e, "lm_head_argmax");
 }
 
+// 2-D uint8 tensor map over the int8 LM head [vocab][1280]: box 128 bytes x kQBoxRows rows, 128B
+// swizzle; rows past the end read as zero.
+static int make_lm_map(CUtensorMap* m, const void* wq, int vocab) {
+  EncodeTiledFn enc = tensor_map_encode_fn();
+  if (!enc) return set_error(FW_ERR_LAUNCH, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHidden), static_cast<cuuint64_t>(vocab)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHidden)};
+  cuuint32_t box[2] = {kQChunk, kQBoxRows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(wq), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FW_ERR_ARG, "tensor map encode failed (%d)", static_cast<int>(r));
+  return FW_OK;
+}
+
+template <bool kLN, bool kFinalize>
+static int launch_lm_head_q(LmParams p, cudaStream_t s, bool pdl) {
+  auto kern = lm_head_q_kernel<kLN, kFinalize>;
+  const int grid = num_sms();
+  p.rows_per_cta = (p.vocab + grid - 1) / grid;
+  if (p.rows_per_cta > kLmMaxRowsPerCta)
+    return set_error(FW_ERR_SHAPE, "lm_head_argmax_q: vocab must be <= %d", kLmMaxRowsPerCta * grid);
+  CUtensorMap map;
+  int rc = make_lm_map(&map, p.wq, p.vocab);
+  if (rc) return rc;
+  cudaError_t e = ensure_smem(kern, kQSmem);
+  if (e == cudaSuccess) e = launch(kern, dim3(grid), dim3(256), kQSmem, s, pdl, map, p);
+  return launch_status(e, "lm_head_argmax_q");
+}
+
 // ---------------------------------------------------------------------------------------------
 // Split-K attention without caller-allocated workspace (fw_decode_attention_noalloc).
 // The fp32 split partials live in this fixed device array instead: per GPU that loads the library,
@@ -1501,6 +1979,35 @@ int fw_lm_head_argmax(const void* h, const void* w, const bool* suppress, int vo
   return launch_lm_head<false, false>(p, static_cast<cudaStream_t>(stream), false);
 }
 
+int fw_lm_quantize(const void* w, int vocab, int hidden, void* wq, void* rp, fw_stream_t stream) {
+  FW_REQUIRE(w && wq && rp, FW_ERR_NULL, "lm_quantize: w, wq and rp are required");
+  FW_REQUIRE(hidden == kHidden, FW_ERR_SHAPE, "hidden size must be %d", kHidden);
+  FW_REQUIRE(vocab > 0, FW_ERR_SHAPE, "lm_quantize: vocab must be positive");
+  FW_REQUIRE(aligned16(w) && aligned16(wq) && aligned16(rp), FW_ERR_ALIGN, "w, wq and rp must be 16-byte aligned");
+  cudaError_t e = launch(lm_quantize_kernel, dim3((vocab + 7) / 8), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                         false, static_cast<const half*>(w), vocab, static_cast<int8_t*>(wq), static_cast<float4*>(rp));
+  return launch_status(e, "lm_quantize");
+}
+
+int fw_lm_head_argmax_q(const void* h, const void* w, const void* wq, const void* rp, const bool* suppress, int vocab,
+                        int hidden, int64_t* best, fw_stream_t stream) {
+  FW_REQUIRE(h && w && wq && rp && suppress && best, FW_ERR_NULL,
+             "lm_head_argmax_q: h, w, wq, rp, suppress and best are required");
+  FW_REQUIRE(hidden == kHidden, FW_ERR_SHAPE, "hidden size must be %d", kHidden);
+  FW_REQUIRE(vocab > 0, FW_ERR_SHAPE, "suppress must be bool [vocab]");
+  FW_REQUIRE(aligned16(h) && aligned16(w) && aligned16(wq) && aligned16(rp), FW_ERR_ALIGN,
+             "h, w, wq and rp must be 16-byte aligned");
+  LmParams p{};
+  p.h = static_cast<const half*>(h);
+  p.w = static_cast<const half*>(w);
+  p.wq = static_cast<const int8_t*>(wq);
+  p.rp = static_cast<const float4*>(rp);
+  p.vocab = vocab;
+  p.mask = suppress;
+  p.best = reinterpret_cast<unsigned long long*>(best);
+  return launch_lm_head_q<false, false>(p, static_cast<cudaStream_t>(stream), false);
+}
+
 int fw_argmax_finalize(int64_t* best, int64_t* tokens, int64_t n_tokens, int64_t* state, int64_t* cur, int max_pos,
                        fw_stream_t stream) {
   FW_REQUIRE(best && tokens && state && cur, FW_ERR_NULL, "argmax_finalize: best, tokens, state and cur are required");
@@ -1598,6 +2105,9 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
                  d->counters && d->cur && d->state && d->tokens && d->best,
              FW_ERR_NULL, "decoder_step: a required pointer is NULL");
   FW_REQUIRE(d->prompt_len == 0 || d->prompt != nullptr, FW_ERR_NULL, "decoder_step: prompt is NULL");
+  FW_REQUIRE((d->lm_q == nullptr) == (d->lm_rp == nullptr), FW_ERR_NULL, "decoder_step: set both lm_q and lm_rp or neither");
+  FW_REQUIRE(d->lm_q == nullptr || (aligned16(d->lm_q) && aligned16(d->lm_rp)), FW_ERR_ALIGN,
+             "decoder_step: lm_q and lm_rp must be 16-byte aligned");
   const int self_splits = (d->max_pos + kSplitKeys - 1) / kSplitKeys;
   const int cross_splits = (d->enc_len + kSplitKeys - 1) / kSplitKeys;
   FW_REQUIRE(self_splits <= kHeadCtas && cross_splits <= kHeadCtas * kHeadMaxUnits, FW_ERR_SHAPE,
@@ -1702,7 +2212,14 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
     m.cur = d->cur;
     m.max_pos = d->max_pos;
     m.prompt_len = d->prompt_len;
-    int rc = launch_lm_head<true, true>(m, s, true);
+    int rc;
+    if (d->lm_q != nullptr) {
+      m.wq = static_cast<const int8_t*>(d->lm_q);
+      m.rp = static_cast<const float4*>(d->lm_rp);
+      rc = launch_lm_head_q<true, true>(m, s, true);
+    } else {
+      rc = launch_lm_head<true, true>(m, s, true);
+    }
     if (rc) return rc;
   }
   return FW_OK;

@@ -2,6 +2,7 @@
 // properties and the per-kernel shared-memory opt-in.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -39,6 +40,12 @@ inline cudaError_t ensure_smem(K kernel, int bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
   return ensure_smem_raw(reinterpret_cast<const void*>(kernel), bytes);
 }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (nullptr if unavailable).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encode_fn();
 
 // Device error words of each translation unit (defined next to the kernels).
 unsigned int read_decode_errors(bool clear);

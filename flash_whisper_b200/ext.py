@@ -99,6 +99,32 @@ class Ext:
         _check(best.dtype == torch.long and best.numel() == 1 and best.is_cuda, 'best must be int64 [1]')
         _lib.call('fw_lm_head_argmax', _ptr(h), _ptr(w), _ptr(suppress), w.size(0), HIDDEN, _ptr(best), _stream())
 
+    def lm_quantize(self, w):
+        """(wq int8 [vocab, 1280], rp fp32 [vocab, 4]): the int8 LM head and per-row bounds that
+        lm_head_argmax_q and the decode step's pruned argmax stream instead of w."""
+        _check_half(w, 'w')
+        _check(w.dim() == 2 and w.size(1) == HIDDEN, f'hidden size must be {HIDDEN}')
+        wq = torch.empty(w.shape, dtype=torch.int8, device=w.device)
+        rp = torch.empty(w.size(0), 4, dtype=torch.float32, device=w.device)
+        _lib.call('fw_lm_quantize', _ptr(w), w.size(0), HIDDEN, _ptr(wq), _ptr(rp), _stream())
+        return wq, rp
+
+    def lm_head_argmax_q(self, h, w, wq, rp, suppress, best):
+        """As lm_head_argmax (same key), streaming the lm_quantize output and recomputing exactly
+        only the rows that can still win."""
+        _check_half(h, 'h')
+        _check_half(w, 'w')
+        _check(h.numel() == HIDDEN and w.dim() == 2 and w.size(1) == HIDDEN, f'hidden size must be {HIDDEN}')
+        _check(wq.dtype == torch.int8 and wq.shape == w.shape and wq.is_cuda and wq.is_contiguous(),
+               'wq must be int8 like w')
+        _check(rp.dtype == torch.float32 and rp.shape == (w.size(0), 4) and rp.is_cuda and rp.is_contiguous(),
+               'rp must be fp32 [vocab, 4]')
+        _check(suppress.dtype == torch.bool and suppress.numel() == w.size(0) and suppress.is_cuda
+               and suppress.is_contiguous(), 'suppress must be bool [vocab]')
+        _check(best.dtype == torch.long and best.numel() == 1 and best.is_cuda, 'best must be int64 [1]')
+        _lib.call('fw_lm_head_argmax_q', _ptr(h), _ptr(w), _ptr(wq), _ptr(rp), _ptr(suppress), w.size(0), HIDDEN,
+                  _ptr(best), _stream())
+
     def argmax_finalize(self, best, tokens, state, cur, max_pos):
         """Appends the decoded token, feeds it back, advances the position and resets best."""
         _check(tokens.dtype == torch.long and state.dtype == torch.long and cur.dtype == torch.long,

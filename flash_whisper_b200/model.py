@@ -64,7 +64,7 @@ def _load_pretrained(model_id, cache_dir):
 class CustomModel:
     @torch.inference_mode()
     def __init__(self, model_id=None, cache_dir=None, *, state_dict=None, dims=None, seed=0, tokenizer=None,
-                 chunk=CHUNK, selftest=True, capture=True):
+                 chunk=CHUNK, selftest=True, capture=True, lm_prune=True):
         if not torch.cuda.is_available():
             raise RuntimeError('CustomModel requires a CUDA device')
         self.ext = load_ext()
@@ -80,6 +80,9 @@ class CustomModel:
         dev, half = 'cuda', torch.float16
         self.dec = pack_decoder(state_dict, dims, dev)
         self.enc = pack_encoder(state_dict, dims, dev)
+        # int8 copy of the LM head with per-row bounds: each step streams it and rescores exactly only
+        # the rows that can still win (fw_lm_head_argmax_q; the chosen token is unchanged)
+        self.lm_q, self.lm_rp = self.ext.lm_quantize(self.dec.lm_head) if lm_prune else (None, None)
         self.heads, self.head_dim = dims.heads, dims.head_dim
         self.scale = self.head_dim ** -0.5
         self.max_pos, self.enc_len = dims.max_pos, dims.enc_len
@@ -169,6 +172,8 @@ class CustomModel:
         desc.ws_splits = self.splits
         desc.counters, desc.cur, desc.state = _p(self.counters), _p(self.cur), _p(self.state)
         desc.tokens, desc.best, desc.n_tokens = _p(self.tokens), _p(self.best), self.tokens.numel()
+        if self.lm_q is not None:
+            desc.lm_q, desc.lm_rp = _p(self.lm_q), _p(self.lm_rp)
         return desc
 
     def _encoder_desc(self):

@@ -92,6 +92,20 @@ int fw_decode_attention_noalloc(const void* q, void* k, void* v, void* out, cons
 int fw_lm_head_argmax(const void* h, const void* w, const bool* suppress, int vocab, int hidden, int64_t* best,
                       fw_stream_t stream);
 
+/* Packs an fp16 LM head w [vocab, hidden] for fw_lm_head_argmax_q: wq int8 [vocab, hidden] (row r =
+ * round(w[r] / s_r), s_r = max|w[r]| / 127) and rp float4 [vocab] = {s_r, a_r, c2_r, 0} with
+ * a_r >= max_i |w[r,i] - s_r wq[r,i]| + 1e-5 max_i |w[r,i]| and c2_r >= 0.51 s_r sum_i |wq[r,i]|
+ * (computed in fp64, rounded up). Run once per weight set. No reference counterpart: the
+ * reference streams the fp16 matrix every step (whisper_kernels.cu:30-86). */
+int fw_lm_quantize(const void* w, int vocab, int hidden, void* wq, void* rp, fw_stream_t stream);
+
+/* Same contract and result as fw_lm_head_argmax (bit-identical best key) with half the bytes read:
+ * streams wq/rp from fw_lm_quantize, bounds every row's fp32 logit, and recomputes exactly (the
+ * fw_lm_head_argmax arithmetic) only the rows whose upper bound reaches the best lower bound of
+ * their block of rows. w is the fp16 matrix wq was made from. */
+int fw_lm_head_argmax_q(const void* h, const void* w, const void* wq, const void* rp, const bool* suppress,
+                        int vocab, int hidden, int64_t* best, fw_stream_t stream);
+
 /* Decodes best into a token, appends it to tokens[state[1]] (when state[1] < max_pos and
  * < n_tokens), feeds it back into cur, advances state[0] (capped at max_pos-1) and resets best.
  * Replaces argmax_finalize, custom/kernels/whisper_kernels.cu:291-298 (kernel :90-100). */
@@ -163,6 +177,9 @@ typedef struct {
   unsigned int* counters;                   /* [heads + 1], zero before the first step; left zero */
   int64_t *cur, *state, *tokens, *best;     /* [1], [2] = {position, count}, [n_tokens], [1] (0) */
   int64_t n_tokens;
+  const void *lm_q, *lm_rp;                 /* optional (both or neither): fw_lm_quantize output for
+                                               lm_head; when set, each step's argmax streams these and
+                                               rescores the rows that can still win (same token) */
 } fw_decoder_t;
 
 /* Launches `steps` decode steps. Step semantics follow custom/model.py:107-123 and :197-207:

@@ -107,3 +107,52 @@ def linear(x, w, b=None):
     if b is not None:
         y = y + np.asarray(b, np.float16).astype(np.float64)
     return f16(y)
+
+
+def lm_quantize(w):
+    """Checker for fw_lm_quantize (no reference counterpart: the reference streams the fp16 LM head
+    every step, custom/kernels/whisper_kernels.cu:30-86). Per row: s = fp32(max|w| / 127) (1 for an
+    all-zero row), q = rint(fp32(w / s)) clipped to +-127, a = max|w - s q| + 1e-5 max|w|,
+    c2 = 0.51 s sum|q|, both in float64 (the device rounds them up to fp32)."""
+    w32 = np.asarray(w, np.float16).astype(np.float32)
+    wmax = np.abs(w32).max(1)
+    s = np.where(wmax > 0, wmax / np.float32(127), np.float32(1)).astype(np.float32)
+    q = np.clip(np.rint(w32 / s[:, None]), -127, 127).astype(np.int8)
+    err = np.abs(w32.astype(np.float64) - q.astype(np.float64) * s[:, None].astype(np.float64)).max(1)
+    a = err + 1e-5 * wmax.astype(np.float64)
+    c2 = 0.51 * s.astype(np.float64) * np.abs(q.astype(np.int64)).sum(1)
+    return q, s, a, c2
+
+
+def lm_bounds(x, q, s, a, c2, xq_max=8191):
+    """The pass-1 quantities of the pruned LM head for fp16 x: (approx, bound) per row, float64,
+    such that |w_r . x - approx_r| <= bound_r (fp32 rounding slack of the device omitted)."""
+    x = np.asarray(x, np.float16).astype(np.float64).reshape(-1)
+    xmax = np.abs(x).max()
+    sx = xmax / xq_max if xmax > 0 else 0.0
+    xq = np.clip(np.rint(x / sx), -xq_max, xq_max) if xmax > 0 else np.zeros_like(x)
+    S = q.astype(np.int64) @ xq.astype(np.int64)
+    approx = s.astype(np.float64) * sx * S
+    bound = np.abs(x).sum() * a + sx * c2 + 4e-7 * np.abs(approx)
+    return approx, bound
+
+
+def lm_prune_rows(approx, bound, suppress, rows_per_block):
+    """Rows kept for exact rescoring: per block of rows_per_block rows, U_r >= T - m with
+    T = max L_r over unsuppressed rows and m = 2^-9 (|T| + 2 max bound) + 2^-23 (every unsuppressed
+    row of the block when |T| >= 32768 or T is not finite)."""
+    keep = np.zeros(approx.size, bool)
+    sup = np.asarray(suppress, bool)
+    for b0 in range(0, approx.size, rows_per_block):
+        sl = slice(b0, min(approx.size, b0 + rows_per_block))
+        ok = ~sup[sl]
+        if not ok.any():
+            continue
+        lo, hi = approx[sl] - bound[sl], approx[sl] + bound[sl]
+        t = lo[ok].max()
+        bm = bound[sl][ok].max()
+        if not np.isfinite(t) or abs(t) >= 32768 or not bm < 32768:
+            keep[sl] = ok
+            continue
+        keep[sl] = ok & (hi >= t - (2.0 ** -9 * (abs(t) + 2 * bm) + 2.0 ** -23))
+    return keep

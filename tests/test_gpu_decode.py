@@ -110,6 +110,72 @@ def test_lm_head_argmax_ties_go_to_lower_index(ext):
     assert K.unpack_index(int(best) & 0xFFFFFFFFFFFFFFFF) == 50000
 
 
+def test_lm_quantize_matches_oracle(ext):
+    g = torch.Generator(device='cuda').manual_seed(11)
+    w = (torch.randn(4096, HIDDEN, device='cuda', generator=g) * 0.02).half()
+    w[17] = 0
+    wq, rp = ext.lm_quantize(w)
+    q, s, a, c2 = K.lm_quantize(w.cpu().numpy())
+    assert np.array_equal(wq.cpu().numpy(), q)
+    rp = rp.cpu().numpy()
+    assert np.array_equal(rp[:, 0], s)
+    for col, want in ((1, a), (2, c2)):  # rounded up from the float64 value: >= it and < one fp32 step above
+        got = rp[:, col].astype(np.float64)
+        assert np.all(got >= want)
+        assert np.all(got <= np.nextafter(want.astype(np.float32), np.float32(np.inf)).astype(np.float64))
+
+
+def _best_pair(ext, h, w, wq, rp, sup):
+    b, bq = torch.zeros(1, device='cuda', dtype=torch.long), torch.zeros(1, device='cuda', dtype=torch.long)
+    ext.lm_head_argmax(h, w, sup, b)
+    ext.lm_head_argmax_q(h, w, wq, rp, sup, bq)
+    return int(b), int(bq)
+
+
+def test_lm_head_argmax_q_equals_exact_kernel(ext, ref_ext):
+    """Same packed key as the full fp16 LM head (itself bit-exact with the reference kernel) on
+    LayerNorm-like inputs, suppressed rows, planted fp16 ties, a zero input and overflowing logits."""
+    g = torch.Generator(device='cuda').manual_seed(12)
+    w = (torch.randn(VOCAB, HIDDEN, device='cuda', generator=g) * 0.02).half()
+    wq, rp = ext.lm_quantize(w)
+    for trial in range(6):
+        h = torch.randn(HIDDEN, device='cuda', generator=g)
+        h = ((h - h.mean()) / h.std()).half().view(1, HIDDEN)
+        sup = torch.rand(VOCAB, device='cuda', generator=g) < 0.01
+        b, bq = _best_pair(ext, h, w, wq, rp, sup)
+        assert b == bq
+        if trial == 0:
+            br = torch.zeros(1, device='cuda', dtype=torch.long)
+            ref_ext.lm_head_argmax(h, w, sup, br)
+            assert bq == int(br)
+    # ties: copies of the winning row in other blocks of rows; the lowest index must win
+    h = torch.randn(1, HIDDEN, device='cuda', generator=g).half()
+    none = torch.zeros(VOCAB, dtype=torch.bool, device='cuda')
+    top = K.unpack_index(_best_pair(ext, h, w, wq, rp, none)[0] & 0xFFFFFFFFFFFFFFFF)
+    w2 = w.clone()
+    for r in (3, 20000, 51000):
+        w2[r] = w2[top]
+    wq2, rp2 = ext.lm_quantize(w2)
+    b, bq = _best_pair(ext, h, w2, wq2, rp2, none)
+    assert b == bq and K.unpack_index(bq & 0xFFFFFFFFFFFFFFFF) == min(3, top)
+    if top != 3:
+        sup = none.clone()
+        sup[3] = True
+        b, bq = _best_pair(ext, h, w2, wq2, rp2, sup)
+        assert b == bq and K.unpack_index(bq & 0xFFFFFFFFFFFFFFFF) == min(20000, top)
+    # zero input: every logit is 0, the first unsuppressed row wins
+    sup = none.clone()
+    sup[:5] = True
+    b, bq = _best_pair(ext, torch.zeros(1, HIDDEN, device='cuda', dtype=torch.float16), w, wq, rp, sup)
+    assert b == bq and K.unpack_index(bq & 0xFFFFFFFFFFFFFFFF) == 5
+    # logits beyond the fp16 range tie at +inf
+    w3 = (torch.randn(VOCAB, HIDDEN, device='cuda', generator=g) * 6).half()
+    wq3, rp3 = ext.lm_quantize(w3)
+    h = (torch.randn(1, HIDDEN, device='cuda', generator=g) * 60).half()
+    b, bq = _best_pair(ext, h, w3, wq3, rp3, none)
+    assert b == bq
+
+
 def test_argmax_finalize_bookkeeping(ext):
     key = int(K.pack_score(0.75, 4321))
     best = torch.tensor([key - (1 << 64) if key >= 1 << 63 else key], dtype=torch.long, device='cuda')
