@@ -1122,6 +1122,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   __shared__ float warp_l[8], warp_b[8], xstat[2][8];
   __shared__ unsigned long long warp_best[8];
   __shared__ int ncand;
+  __shared__ unsigned s_lo_max;  // running max of the lower bounds (order-preserving bits)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* stages = smem_raw + (base - raw);
@@ -1166,7 +1167,10 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
     rps[i] = p.rp[r0 + i];
   }
   for (int i = threadIdx.x; i < kQXBytes / 16; i += 256) reinterpret_cast<uint4*>(xb)[i] = make_uint4(0, 0, 0, 0);
-  if (threadIdx.x == 0) ncand = 0;
+  if (threadIdx.x == 0) {
+    ncand = 0;
+    s_lo_max = float_to_ordered(-INFINITY);
+  }
   float g[5], be[5];
   if (kLN) {
 #pragma unroll
@@ -1324,6 +1328,12 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
           lmax = fmaxf(lmax, approx - b);
           bmax = fmaxf(bmax, b);
           if (!isfinite(approx) || !isfinite(b)) bmax = INFINITY;
+          // Rows that may survive the selection (against the lower bounds seen so far) have their
+          // fp16 row fetched into L2 now, so the exact pass reads them from L2. A hint only.
+          const float lo = approx - b;
+          const float run = fmaxf(ordered_to_float(atomicMax(&s_lo_max, float_to_ordered(lo))), lo);
+          if (approx + b >= run - (0x1p-9f * (fabsf(run) + 2.f * b) + 0x1p-23f))
+            l2_prefetch(p.w + static_cast<size_t>(r0 + li) * kHidden, kHidden * 2);
         }
       }
     }
@@ -1353,19 +1363,24 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   }
   __syncthreads();
 
-  // ---- pass 2: exact fp16 logits of the surviving rows, two rows per warp at a time ----
+  // ---- pass 2: exact fp16 logits of the surviving rows, four rows per warp at a time ----
   const int nc = ncand;
   unsigned long long mine = 0;
-  for (int j = 2 * warp; j < nc; j += 16) {
-    const int ra = r0 + cand[j];
-    const int rb = j + 1 < nc ? r0 + cand[j + 1] : ra;
-    const half* rows[2] = {p.w + static_cast<size_t>(ra) * kHidden, p.w + static_cast<size_t>(rb) * kHidden};
-    float acc[2];
-    dot1280_ptrs<2>(rows, xf, acc);
-    const unsigned long long ka = pack_score(round_half(acc[0]), ra);
-    const unsigned long long kb = pack_score(round_half(acc[1]), rb);
-    mine = ka > mine ? ka : mine;
-    mine = kb > mine ? kb : mine;
+  for (int j = 4 * warp; j < nc; j += 32) {
+    int rr[4];
+    const half* rows[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      rr[q] = r0 + cand[min(j + q, nc - 1)];  // a repeated row repeats its key
+      rows[q] = p.w + static_cast<size_t>(rr[q]) * kHidden;
+    }
+    float acc[4];
+    dot1280_ptrs<4>(rows, xf, acc);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const unsigned long long k = pack_score(round_half(acc[q]), rr[q]);
+      mine = k > mine ? k : mine;
+    }
   }
   if (lane == 0) warp_best[warp] = mine;
   tc_fence_before();
