@@ -47,8 +47,9 @@ N_CLIPS = 256
 TOKENS_PER_SECOND = 7.5
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one lm_head_q_kernel launch from an ncu capture of
-# the decode step (profiles/lm_head_q_decode_step.txt); None until captured.
-LM_HEAD_TRAFFIC_BYTES = None
+# the decode step (profiles/lm_head_q_decode_step.txt): 76.11 MB read (67.3 MB algorithmic + rescored
+# and L2-prefetched fp16 rows) + 1.15 MB written.
+LM_HEAD_TRAFFIC_BYTES = 76_108_032 + 1_145_088
 
 
 def peaks():
