@@ -43,6 +43,35 @@ def test_decoder_struct_matches_header_layout():
     assert ctypes.sizeof(_lib.DecoderLayer) == 22 * 8
     assert _lib.Decoder.layers.offset == 8 * 4 + 8 * 8
     assert ctypes.sizeof(_lib.EncoderLayer) == 12 * 8
+    assert _lib.Decoder.lm_q.offset == _lib.Decoder.n_tokens.offset + 8
+    assert _lib.Decoder.lm_rp.offset == _lib.Decoder.lm_q.offset + 8
+    assert ctypes.sizeof(_lib.Decoder) == _lib.Decoder.lm_rp.offset + 8
+
+
+def test_pruned_lm_head_argument_checks():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+    assert lib.fw_lm_quantize(None, 51866, 1280, p, p, None) == 1
+    assert b'required' in lib.fw_last_error_string()
+    assert lib.fw_lm_quantize(p, 51866, 1024, p, p, None) == 2
+    assert b'hidden size must be 1280' in lib.fw_last_error_string()
+    assert lib.fw_lm_quantize(ctypes.c_void_p(18), 51866, 1280, p, p, None) == 3  # FW_ERR_ALIGN
+    assert lib.fw_lm_head_argmax_q(p, p, None, p, p, 51866, 1280, p, None) == 1
+    assert b'wq' in lib.fw_last_error_string()
+    assert lib.fw_lm_head_argmax_q(p, p, p, p, p, 0, 1280, p, None) == 2
+
+
+def test_decoder_step_needs_both_pruned_lm_buffers():
+    lib = _lib.lib()
+    d = _lib.Decoder()
+    d.n_layers, d.heads, d.max_pos, d.enc_len, d.vocab = 4, 20, 448, 1500, 51866
+    d.ws_splits = 24
+    for name in ('embed', 'pos_embed', 'lm_head', 'final_g', 'final_b', 'h', 'ffn', 'part_acc', 'counters', 'cur',
+                 'state', 'tokens', 'best'):
+        setattr(d, name, 16)
+    d.lm_q = 16  # lm_rp left NULL
+    assert lib.fw_decoder_step(ctypes.byref(d), 1, None) == 1
+    assert b'set both lm_q and lm_rp' in lib.fw_last_error_string()
 
 
 def test_wrapper_checks_mirror_reference_messages():
