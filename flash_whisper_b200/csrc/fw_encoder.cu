@@ -11,18 +11,23 @@
 //    accumulator back with tcgen05.ld and run the fused epilogue (bias, GELU, residual add,
 //    positions, q scaling, cross-K/V scatter). Weight tiles of the first stages are requested
 //    before the PDL wait.
+//  * gemm_splitk2_kernel: for long K, a 2-CTA cluster splits K of one 128 x 256 tile and exchanges
+//    the fp32 halves over DSMEM before the epilogue.
 //  * Conv1d(k=3, pad=1) runs as the same GEMM: the time-major input carries one zero row at each
 //    end and a 3-D tensor map [rows/stride, stride, C] lets the producer fetch tap j of output rows
 //    t0..t0+127 (input rows stride*t + j) as one box, so no im2col buffer is materialised.
 //  * enc_attention_kernel: bidirectional attention, 128 queries x one head per CTA, online
 //    softmax over 64-key blocks, QK^T and PV on mma.sync m16n8k16 with ldmatrix from swizzled
 //    shared memory, K/V double-buffered with cp.async.
+#include <cooperative_groups.h>
 #include <cuda.h>
 
 #include "fw_common.cuh"
 #include "fw_host.h"
 
 namespace fw {
+
+namespace cg = cooperative_groups;
 
 FW_DEFINE_ERROR_WORD();
 
@@ -331,6 +336,184 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Split-K GEMM for long K: a cluster of two CTAs computes one 128 x 256 tile, CTA r accumulating
+// k-blocks r * num_kb / 2 .. (r + 1) * num_kb / 2 - 1 in its own TMEM (N = 256 MMAs). After both
+// mainloops each CTA writes the 128 columns its peer finishes (fp32, column-major 128 x 128, 64 KB)
+// into the peer's now idle stage ring through DSMEM; after a second cluster barrier each CTA adds
+// the received half to its own and runs the epilogue on its 128 columns. One tile per cluster, one
+// round (the dispatcher uses it only when 2 x tiles CTAs fit on the GPU).
+template <int STAGES, bool kConv>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_splitk2_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                              const __grid_constant__ CUtensorMap tmB, int num_kb,
+                                                              int conv_c, int conv_stride, GemmEpi ep, int m_tiles,
+                                                              const char* l2_next, unsigned l2_bytes) {
+  constexpr int BM = 128, BK = 64, BN = 256, kHalf = BN / 2;
+  constexpr uint32_t kABytes = BM * BK * 2;
+  constexpr uint32_t kBBytes = BN * BK * 2;
+  constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static_assert(STAGES * kStageBytes >= kHalf * BM * 4, "the exchange buffer lives in the stage ring");
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ __align__(16) uint4 s_bias[kHalf / 8];
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  float* xbuf = reinterpret_cast<float*>(smem);  // after the mainloop: [kHalf columns][BM rows] from the peer
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int peer = rank ^ 1;
+  const int tile = static_cast<int>(blockIdx.x) >> 1;
+  const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
+  const int nkb = num_kb / 2, kb0 = rank * nkb;
+  const int pre = nkb < STAGES ? nkb : STAGES;
+
+  if (warp == 0 && lane == 0) {
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full_bar[st], 1);
+      mbar_init(&empty_bar[st], 1);
+    }
+    mbar_init(&acc_full, 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int i = 0; i < pre; ++i) {  // weight tiles of the first stages do not depend on the previous kernel
+      mbar_arrive_expect_tx(&full_bar[i], kStageBytes);
+      tma_load_2d(smem + i * kStageBytes + kABytes, &tmB, &full_bar[i], (kb0 + i) * BK, n0);
+    }
+    if (l2_next != nullptr && l2_bytes > 0) {
+      const unsigned share = ((l2_bytes + gridDim.x - 1) / gridDim.x + 15u) & ~15u;
+      const unsigned off = share * blockIdx.x;
+      if (off < l2_bytes) {
+        const unsigned n = min(share, l2_bytes - off);
+        for (unsigned o = 0; o < n; o += 65536u) l2_prefetch(l2_next + off + o, min(65536u, n - o));
+      }
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  // epilogue-thread state prepared while the mainloop runs
+  const int q = warp & 3, hid = (warp - 2) >> 2;  // warps 2..9: TMEM lane quadrant, 64-column half
+  const int row = m0 + q * 32 + lane;
+  const bool row_ok = warp >= 2 && row < ep.M;
+  uint4 res[8] = {};
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      pdl_wait();
+      pdl_trigger();
+      for (int i = 0; i < nkb; ++i) {
+        const int st = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1u;
+        uint8_t* sa = smem + st * kStageBytes;
+        if (i >= pre) {
+          if (!mbar_wait(&empty_bar[st], ph ^ 1u)) {
+            enc_flag(FW_DEVERR_TIMEOUT);
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[st], kStageBytes);
+          tma_load_2d(sa + kABytes, &tmB, &full_bar[st], (kb0 + i) * BK, n0);
+        }
+        if (kConv) {
+          const int k = (kb0 + i) * BK;
+          const int tap = k / conv_c;
+          const int c0 = k - tap * conv_c;
+          tma_load_3d(sa, &tmA, &full_bar[st], c0, tap % conv_stride, m0 + tap / conv_stride);
+        } else {
+          tma_load_2d(sa, &tmA, &full_bar[st], (kb0 + i) * BK, m0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int st = i % STAGES;
+        if (!mbar_wait(&full_bar[st], (i / STAGES) & 1u)) {
+          enc_flag(FW_DEVERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = base + st * kStageBytes;
+        const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(a_addr + kABytes);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) tc_mma_f16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0);
+        tc_commit(&empty_bar[st]);
+      }
+      tc_commit(&acc_full);
+    }
+  } else {
+    pdl_wait();
+    const int et = threadIdx.x - 64;
+    if (ep.bias != nullptr && et < kHalf / 8)
+      s_bias[et] = __ldg(reinterpret_cast<const uint4*>(ep.bias + n0 + rank * kHalf) + et);
+    if (row_ok && epi_reads_r(ep.mode)) {
+      const uint4* r4 = reinterpret_cast<const uint4*>(ep.R + static_cast<size_t>(row) * ep.ldr + n0 + rank * kHalf +
+                                                       hid * 64);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) res[i] = r4[i];
+    }
+    ok = mbar_wait_warp(&acc_full, 0);
+    if (!ok) enc_flag(FW_DEVERR_TIMEOUT);
+  }
+  // 1: both CTAs' MMAs are complete (every epilogue warp saw acc_full), so both stage rings are idle
+  tc_fence_before();
+  cluster.sync();
+  tc_fence_after();
+  if (warp >= 2 && ok) {
+    float* px = cluster.map_shared_rank(xbuf, peer);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+    for (int p4 = 0; p4 < 4; ++p4) {
+      const int c = hid * 64 + p4 * 16;  // column within the peer's half
+      uint32_t r[16];
+      tc_ld16(lane_base + static_cast<uint32_t>(peer * kHalf + c), r);
+      tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) px[(c + j) * BM + q * 32 + lane] = __uint_as_float(r[j]);
+    }
+  }
+  // 2: the peer's partial of this CTA's columns is in xbuf
+  tc_fence_before();
+  cluster.sync();
+  tc_fence_after();
+  if (warp >= 2 && ok) {
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll
+    for (int p4 = 0; p4 < 4; ++p4) {
+      const int c = hid * 64 + p4 * 16;  // column within this CTA's half
+      uint32_t r[16];
+      tc_ld16(lane_base + static_cast<uint32_t>(rank * kHalf + c), r);
+      tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        r[j] = __float_as_uint(__uint_as_float(r[j]) + xbuf[(c + j) * BM + q * 32 + lane]);
+      if (row_ok)
+        epilogue_store16(ep, row, n0 + rank * kHalf + c, r, ep.bias != nullptr ? s_bias + c / 8 : nullptr,
+                         res[2 * p4], res[2 * p4 + 1]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
   }
 }
 
@@ -715,6 +898,26 @@ static int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int K, in
   return launch_status(e, "gemm_tc");
 }
 
+template <int STAGES, bool kConv>
+static int launch_splitk2_t(const CUtensorMap& ta, const CUtensorMap& tb, int K, int conv_c, int conv_stride,
+                            const GemmEpi& ep, const void* l2_next, size_t l2_bytes, cudaStream_t s, bool pdl) {
+  constexpr int smem = STAGES * (128 * 64 * 2 + 256 * 64 * 2) + 1024;
+  auto kern = gemm_splitk2_kernel<STAGES, kConv>;
+  cudaError_t e = ensure_smem(kern, smem);
+  if (e == cudaSuccess) {
+    const int m_tiles = (ep.M + 127) / 128, tiles = m_tiles * (ep.N / 256);
+    e = launch_cluster(kern, dim3(2 * tiles), dim3(kGemmThreads), smem, s, pdl, 2u, ta, tb, K / 64, conv_c,
+                       conv_stride, ep, m_tiles, static_cast<const char*>(l2_next), static_cast<unsigned>(l2_bytes));
+  }
+  return launch_status(e, "gemm_splitk2");
+}
+
+// Long-K GEMMs whose 128 x 256 tiles, split in two along K, fit on the GPU in one round.
+static bool use_splitk2(int M, int N, int K) {
+  const int kb = K / 64;
+  return kb >= 40 && kb % 2 == 0 && N % 256 == 0 && 2 * ((M + 127) / 128) * (N / 256) <= num_sms();
+}
+
 // Picks the N tile: the fewest tile rounds per SM, weighted by the tile width (a round costs time
 // proportional to BN) and by the lower tensor efficiency of narrow tiles. The 320-wide tile has a
 // single TMEM accumulator (its epilogue cannot overlap a next tile), so it is used only when every
@@ -742,6 +945,13 @@ static int pick_bn(int M, int N) {
 static int gemm_dispatch(const CUtensorMap& ta, const void* B, int64_t ldb, int K, int conv_c, int conv_stride,
                          bool conv, const GemmEpi& ep, const void* l2_next, size_t l2_bytes, cudaStream_t s,
                          bool pdl) {
+  if (use_splitk2(ep.M, ep.N, K)) {
+    CUtensorMap tb;
+    int rc = make_map_2d(&tb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(ep.N), static_cast<uint64_t>(ldb), 256);
+    if (rc) return rc;
+    return conv ? launch_splitk2_t<4, true>(ta, tb, K, conv_c, conv_stride, ep, l2_next, l2_bytes, s, pdl)
+                : launch_splitk2_t<4, false>(ta, tb, K, 0, 1, ep, l2_next, l2_bytes, s, pdl);
+  }
   const int bn = pick_bn(ep.M, ep.N);
   CUtensorMap tb;
   int rc = make_map_2d(&tb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(ep.N), static_cast<uint64_t>(ldb),
