@@ -16,9 +16,9 @@
 //  * Conv1d(k=3, pad=1) runs as the same GEMM: the time-major input carries one zero row at each
 //    end and a 3-D tensor map [rows/stride, stride, C] lets the producer fetch tap j of output rows
 //    t0..t0+127 (input rows stride*t + j) as one box, so no im2col buffer is materialised.
-//  * enc_attention_kernel: bidirectional attention, 128 queries x one head per CTA, online
-//    softmax over 64-key blocks, QK^T and PV on mma.sync m16n8k16 with ldmatrix from swizzled
-//    shared memory, K/V double-buffered with cp.async.
+//  * enc_attn_tc_kernel: bidirectional attention, 128 queries x one head per CTA, online softmax
+//    over 64-key blocks; S = QK^T and O += PV^T on tcgen05 with S and O in TMEM, Q / K / V^T tiles
+//    staged by TMA, one thread per query row for the softmax.
 #include <cooperative_groups.h>
 #include <cuda.h>
 
@@ -915,7 +915,7 @@ static int launch_splitk2_t(const CUtensorMap& ta, const CUtensorMap& tb, int K,
 // Long-K GEMMs whose 128 x 256 tiles, split in two along K, fit on the GPU in one round.
 static bool use_splitk2(int M, int N, int K) {
   const int kb = K / 64;
-  return kb >= 40 && kb % 2 == 0 && N % 256 == 0 && 2 * ((M + 127) / 128) * (N / 256) <= num_sms();
+  return kb >= 20 && kb % 2 == 0 && N % 256 == 0 && 2 * ((M + 127) / 128) * (N / 256) <= num_sms();
 }
 
 // Picks the N tile: the fewest tile rounds per SM, weighted by the tile width (a round costs time
