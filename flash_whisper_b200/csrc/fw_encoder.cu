@@ -522,12 +522,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_splitk2_kernel(const __g
 __global__ void __launch_bounds__(256) layernorm_rows_kernel(const half* __restrict__ x, const half* __restrict__ g,
                                                              const half* __restrict__ b, half* __restrict__ y,
                                                              int rows, int cols, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nc = cols / 256;  // 16-byte chunks per lane
+  // gamma and beta are weights: loaded before the wait
+  uint4 gw[8], bw[8];
+  const uint4* g4 = reinterpret_cast<const uint4*>(g);
+  const uint4* b4 = reinterpret_cast<const uint4*>(b);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c < nc) {
+      gw[c] = __ldg(g4 + lane + 32 * c);
+      bw[c] = __ldg(b4 + lane + 32 * c);
+    }
+  }
   pdl_wait();
   pdl_trigger();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= rows) return;
-  const int nc = cols / 256;  // 16-byte chunks per lane
   const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * cols);
   float v[64];
   float sum = 0.f;
@@ -557,14 +568,11 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const half* __restr
   sq = warp_sum(sq);
   const float inv = rsqrtf(sq / cols + eps);
   uint4* yr = reinterpret_cast<uint4*>(y + static_cast<size_t>(row) * cols);
-  const uint4* g4 = reinterpret_cast<const uint4*>(g);
-  const uint4* b4 = reinterpret_cast<const uint4*>(b);
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     if (c < nc) {
-      const uint4 gu = __ldg(g4 + lane + 32 * c), bu = __ldg(b4 + lane + 32 * c);
-      const half* gh = reinterpret_cast<const half*>(&gu);
-      const half* bh = reinterpret_cast<const half*>(&bu);
+      const half* gh = reinterpret_cast<const half*>(&gw[c]);
+      const half* bh = reinterpret_cast<const half*>(&bw[c]);
       uint4 out;
       half* oh = reinterpret_cast<half*>(&out);
 #pragma unroll
