@@ -332,7 +332,7 @@ def bench_ours(args, rank, world, local_rank):
                                '30 s clip, greedy forced to 224 tokens',
                    'model': 'whisper-large-v3-turbo architecture, random-init seed 0 (fp16)', 'global_batch': world,
                    'seq_len': N_TOKENS, 'parallelism': f'replicas{world}' if world > 1 else 'single',
-                   'l2': 'working set larger than L2 (347 MB per decode step, 1.26 GB encoder weights)'},
+                   'l2': 'working set larger than L2 (282 MB per decode step, 1.26 GB encoder weights)'},
         'e2e': {'value': round(e2e_ms, 4), 'unit': 'ms', 'h2d_bytes_per_step': 480000 * 4,
                 'd2h_bytes_per_step': N_TOKENS * 8},
         'decode_us_per_token': round(us_per_token, 3),
@@ -437,7 +437,7 @@ def bench_clips(args, rank, world, local_rank):
                    'model': 'whisper-large-v3-turbo architecture, random-init seed 0 (fp16)', 'clips': len(clips),
                    'audio_seconds': round(total_audio, 2), 'tokens': total_tokens,
                    'parallelism': f'replicas{world}' if world > 1 else 'single',
-                   'l2': 'working set larger than L2 (347 MB per decode step, 1.26 GB encoder weights)'},
+                   'l2': 'working set larger than L2 (282 MB per decode step, 1.26 GB encoder weights)'},
         'e2e': {'value': round(total_audio / e2e_s, 2), 'unit': 'audio-s/s',
                 'h2d_bytes_per_step': len(clips) * 480000 * 4, 'd2h_bytes_per_step': total_tokens * 8},
         'rank0_clips': len(mine),
