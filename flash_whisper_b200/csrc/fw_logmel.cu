@@ -20,7 +20,6 @@ constexpr int kHop = 160;
 constexpr int kBins = kNfft / 2 + 1;  // 201
 constexpr int kMels = 128;
 constexpr int kFramesPerCta = 16;
-constexpr int kSpan = kHop * (kFramesPerCta - 1) + kNfft;  // samples staged per CTA
 
 __device__ __forceinline__ int reflect_index(int j, int len) {
   // torch.stft(center=True, pad_mode='reflect'): pad n_fft/2 on each side by reflection
