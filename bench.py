@@ -9,24 +9,37 @@ seeded random-init weights of the large-v3-turbo architecture (no checkpoint off
 Printed metric (BASELINE.json `metric`): batch-1 30 s-clip E2E latency in ms (lower is better).
 `value` is the device time of a step with the waveform already resident in HBM (CUDA events around
 K back-to-back steps, max over ranks); `e2e` times the public API `CustomModel.transcribe(audio)`
-from pinned host audio to host token ids. Extra keys give per-token decode us, encoder / mel ms,
-the HBM roofline of the decode step and of the LM-head kernel, and the CPU baseline.
+from pinned host audio to host token ids. Extra keys:
+  * decode_us_per_token, ttft_ms, stages_ms (mel / encoder / decode);
+  * decode_kernels: every launch of the decode step timed on its own (each block captured 20 times
+    into one CUDA graph, PDL-chained as in the step), with algorithmic bytes and HBM fraction;
+    `roofline` is the block with the largest share of the step, `roofline_lm_head` the LM head;
+  * roofline_decode_step on the 282 MB (int8 LM head) and 347 MB (fp16 LM head) byte counts;
+  * micro: BASELINE configs 1 and 2 (residual+LN, GELU 5120, embedding gather, self attention at
+    L in {1, 64, 224, 448}, cross attention 1500, argmax 51866, log-mel batch 1 and 32);
+  * config4: BASELINE config 4 (256 clips U[5,30] s, round(7.5 tok/s x s) forced tokens) over the
+    N ranks by a static longest-first partition, as batch-1 streams and as the batched decoder;
+  * cpu_baseline: the reference's CPU path (oracle/hf_cpu.py) for full steps on the host cores.
 
-N > 1 (torchrun): every rank runs its own independent clip stream on its own GPU (batch-1 decode does
-not shard; nothing crosses GPUs). The process group is used only for the barrier and the max-over-
-ranks timing reduction outside the timed region.
+N > 1 (torchrun): every rank runs its own clip stream on its own GPU (batch-1 decode does not shard;
+nothing crosses GPUs). A gloo process group on the host carries the barriers and the max-over-ranks
+reductions, outside the timed regions; no NCCL.
 
---impl reference times the reference's own CPU path (custom/pytorch_model.py's greedy loop restated
-for CPU fp32 by oracle/hf_cpu.py) on the host cores on the same config, one bounded sample per step.
+--impl reference times the reference's own CPU path (custom/pytorch_model.py's greedy loop restated for
+CPU fp32 by oracle/hf_cpu.py, transformers' feature extractor and model) on the host cores, on the
+same config: every step is a full 30 s clip with 224 forced tokens.
 
---workload clips256 runs BASELINE config 4 instead: 256 clips (audio seed i, lengths uniform in
-[5, 30] s, zero-padded to 30 s) with round(7.5 tokens/s x seconds) forced tokens each, split over the
-ranks by a static longest-first greedy partition on the forced-token count; the metric is the
-whole-box throughput in audio-seconds per second (total audio / max-over-ranks device time, strong
-scaling: the 256 clips are the same for every N).
+--workload refcuda (run by hand, N=1) times the reference's CUDA backend (oracle/ref_pipeline.py: its
+kernels compiled from source, HF fp16 encoder, cuBLAS projections, its CUDA graphs) against this
+package on the same GPU, weights and audio, and the reference kernels beside this package's on the
+config-1 microbench inputs.
+
+--workload profile --tokens N (a profiler target) runs one transcription eagerly: log-mel, encoder,
+prompt and N decode steps, one launch after another.
 """
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -45,11 +58,16 @@ SECONDS = 30.0
 N_TOKENS = 224
 N_CLIPS = 256
 TOKENS_PER_SECOND = 7.5
+METRIC = 'batch-1 30s-clip E2E latency'
+CONFIG3 = {'workload': 'BASELINE config 3: GPU log-mel + graphed 32-layer encoder + graphed 4-layer decoder, '
+                       '30 s clip, greedy forced to 224 tokens',
+           'model': 'whisper-large-v3-turbo architecture, random-init seed 0', 'global_batch': 1,
+           'seq_len': N_TOKENS, 'l2': 'working set larger than L2 (282 MB per decode step, 1.26 GB encoder weights)'}
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
-# dram__bytes_read.sum + dram__bytes_write.sum of one lm_head_q_kernel launch from an ncu capture of
-# the decode step (profiles/lm_head_q_decode_step.txt): 76.11 MB read (67.3 MB algorithmic + rescored
-# and L2-prefetched fp16 rows) + 1.15 MB written.
-LM_HEAD_TRAFFIC_BYTES = 76_108_032 + 1_145_088
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from the ncu captures in profiles/
+# (decode_attention_blocks.txt, decode_fc1_fc2.txt, lm_head_q_decode_step.txt)
+NCU_TRAFFIC = {'self_block': 13_180_928, 'cross_block': 14_283_776, 'fc1': 13_154_560, 'fc2': 13_139_200,
+               'lm_head': 76_108_032 + 1_145_088}
 
 
 def peaks():
@@ -138,7 +156,8 @@ def partition(clips, world):
 def decode_bytes_per_token(dims, length, lm_pruned=True):
     """Algorithmic HBM bytes of one decode step at self-attention length `length`. With the pruned
     LM head the vocab matrix is read as int8 plus 16 bytes of scale and bounds per row (the fp16
-    rows rescored exactly, about 8 per 351-row block on these weights, are left out)."""
+    rows rescored exactly, about 8 per 351-row block on these weights, are left out); without it,
+    as the reference's fp16 stream."""
     d, f, L = dims.d_model, dims.ffn, dims.decoder_layers
     per_layer = 2 * (3 * d * d + 3 * d + 3 * d * d + 3 * d + 2 * f * d + f + d + 6 * d)  # weights + biases + LN
     cross = L * 2 * dims.heads * dims.enc_len * dims.head_dim * 2
@@ -148,67 +167,284 @@ def decode_bytes_per_token(dims, length, lm_pruned=True):
     return L * per_layer + cross + self_kv + lm + emb
 
 
+def block_bytes(dims, length, pruned=True):
+    """Algorithmic HBM bytes of each launch of the decode step at self-attention length `length`."""
+    d, f, kv = dims.d_model, dims.ffn, dims.heads * dims.head_dim * 2 * 2
+    ln = 2 * d * 2
+    return {
+        'self_block': 2 * (3 * d * d + 3 * d + d * d + d) + ln + kv * length,
+        'cross_block': 2 * (2 * d * d + 2 * d) + ln + kv * dims.enc_len,
+        'fc1': 2 * (f * d + f) + ln,
+        'fc2': 2 * (d * f + d),
+        'lm_head': (dims.vocab * (d + 16) if pruned else dims.vocab * d * 2) + dims.vocab + ln,
+    }
+
+
 def host_threads():
     """All host cores this process may use (torchrun sets OMP_NUM_THREADS=1 for its ranks)."""
     return len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else (os.cpu_count() or 1)
 
 
-def cpu_reference_sample(n_tokens=8, threads=None):
-    """CPU fp32 reference path on a bounded sample: full mel + encoder + n_tokens decode steps.
+def graph_us(fn, iters=20, reps=10):
+    """Device microseconds per fn() call: fn captured `iters` times into one CUDA graph (consecutive
+    launches PDL-chained as in production), replayed `reps` times between CUDA events."""
+    s = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    side.wait_stream(s)
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    s.wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    for _ in range(3):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (iters * reps)
 
-    Returns (e2e_ms extrapolated to N_TOKENS, details)."""
+
+def replay_us(fn, reps=20):
+    """Device microseconds per fn() call (fn replays CUDA graphs), between CUDA events after warm-up."""
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+# ---- CPU reference path ------------------------------------------------------------------------
+def cpu_reference_model(threads):
+    """The reference's CPU path: transformers Whisper (fp32) on the seed-0 weights, one warm-up."""
     from flash_whisper_b200.audio import synthetic_audio
     from flash_whisper_b200.weights import TURBO, load_hf_model, random_state_dict
     from oracle.hf_cpu import transcribe_cpu
-    if threads:
-        torch.set_num_threads(threads)
+    torch.set_num_threads(threads)
     model = load_hf_model(random_state_dict(0, TURBO), TURBO)
     audio = synthetic_audio(0, SECONDS)
-    transcribe_cpu(model, audio[:16000], TURBO, n_tokens=2)  # warm-up (allocator, kernels)
+    transcribe_cpu(model, audio[:16000], TURBO, n_tokens=2)  # allocator and kernels warm
     return model, audio
 
 
-def run_cpu_sample(model, audio, n_tokens):
+def run_cpu_step(model, audio, n_tokens=N_TOKENS):
+    """One full CPU step: feature extraction, encoder and n_tokens greedy steps. Returns (ms, times)."""
     from flash_whisper_b200.weights import TURBO
     from oracle.hf_cpu import transcribe_cpu
     _, t = transcribe_cpu(model, audio, TURBO, n_tokens=n_tokens, begin_suppress=TURBO.begin_suppress)
-    per_tok = t['decode_s'] / max(1, t['n_tokens'])
-    e2e_ms = (t['mel_s'] + t['encoder_s'] + per_tok * N_TOKENS) * 1e3
-    return e2e_ms, t
+    return t['e2e_s'] * 1e3, t
+
+
+CPU_SAMPLE = ('full steps of the reference CPU path (oracle/hf_cpu.py: custom/pytorch_model.py loop, transformers '
+              'WhisperFeatureExtractor + fp32 WhisperForConditionalGeneration): 30 s clip, 224 forced tokens, '
+              'no extrapolation')
 
 
 def bench_reference(args, rank, world):
     if rank != 0:
         return 0
     threads = host_threads()
-    model, audio = cpu_reference_sample(threads=threads)
-    n_sample = 8
-    for _ in range(max(0, min(args.warmup, 1))):
-        run_cpu_sample(model, audio, n_sample)
+    model, audio = cpu_reference_model(threads)
+    for _ in range(args.warmup):
+        run_cpu_step(model, audio)
     vals, details = [], []
     for _ in range(args.steps):
-        v, t = run_cpu_sample(model, audio, n_sample)
+        v, t = run_cpu_step(model, audio)
         vals.append(v)
         details.append(t)
     value = statistics.median(vals)
-    sample = (f'each step: CPU fp32 log-mel + 32-layer encoder of one 30 s clip + {n_sample} greedy decode steps; '
-              f'E2E extrapolated to {N_TOKENS} tokens as mel + encoder + {N_TOKENS} x measured per-token time')
     line = {
-        'impl': 'reference', 'metric': 'batch-1 30s-clip E2E latency', 'value': round(value, 3), 'unit': 'ms',
-        'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(value, 3),
+        'impl': 'reference', 'metric': METRIC, 'value': round(value, 3), 'unit': 'ms', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(statistics.mean(vals), 3),
         'higher_is_better': False, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'BASELINE config 3 on the CPU path (config 0 loop): 30 s clip, 224 forced tokens',
-                   'model': 'whisper-large-v3-turbo architecture, random-init seed 0', 'batch': 1,
-                   'tokens': N_TOKENS},
-        'cpu_baseline': {'value': round(value, 3), 'unit': 'ms', 'cores': threads, 'kind': 'port', 'sample': sample,
-                         'host_cpus': os.cpu_count()},
+        'config': dict(CONFIG3, parallelism=f'replicas{world}' if world > 1 else 'single'),
+        'cpu_baseline': {'value': round(value, 3), 'unit': 'ms', 'cores': threads, 'kind': 'port',
+                         'sample': CPU_SAMPLE, 'host_cpus': os.cpu_count()},
         'e2e': {'value': round(value, 3), 'unit': 'ms', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
-        'stages_ms': {k: round(statistics.median(d[k] for d in details) * 1e3, 3)
-                      for k in ('mel_s', 'encoder_s')},
+        'stages_ms': {k: round(statistics.median(d[k] for d in details) * 1e3, 3) for k in ('mel_s', 'encoder_s')},
         'decode_ms_per_token': round(statistics.median(d['decode_s'] / d['n_tokens'] for d in details) * 1e3, 3),
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---- this package --------------------------------------------------------------------------------
+class Ranks:
+    """Host-side barrier and reductions over the ranks (gloo); trivial for one rank."""
+
+    def __init__(self, world):
+        self.world = world
+
+    def barrier(self):
+        if self.world > 1:
+            torch.distributed.barrier()
+
+    def reduce(self, x, op='max'):
+        if self.world == 1:
+            return x
+        t = torch.tensor([float(x)], dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX if op == 'max' else
+                                     (torch.distributed.ReduceOp.MIN if op == 'min' else torch.distributed.ReduceOp.SUM))
+        return float(t)
+
+
+def decode_kernel_table(model, dims, pk, length=116):
+    """Each launch of the decode step timed on its own at self-attention length `length` (the mean over
+    a 224-token decode), with algorithmic bytes and HBM fraction; the share is us x launches per step."""
+    ext, desc = model.ext, model.dec_desc
+    model.state.copy_(torch.tensor([length - 1, 0]))
+    model.best.zero_()
+    pruned = model.lm_q is not None
+    nb = block_bytes(dims, length, pruned)
+    per_step = {'self_block': dims.decoder_layers, 'cross_block': dims.decoder_layers, 'fc1': dims.decoder_layers,
+                'fc2': dims.decoder_layers, 'lm_head': 1}
+    names = {'self_block': 'head_block_kernel<self> (LN1 + q/k/v + split attention + cache write + out_proj + '
+                           'residual, 20 clusters x 8 CTAs)',
+             'cross_block': 'head_block_kernel<cross> (LN2 + cross q + split attention over 1500 keys + out_proj '
+                            '+ residual, 20 clusters x 8 CTAs)',
+             'fc1': 'ln_gemv_kernel (LN3 + fc1 5120x1280 + GELU)', 'fc2': 'gemv_residual_kernel (fc2 1280x5120 + '
+                                                                        'residual)',
+             'lm_head': ('lm_head_q_kernel (final LN + int8 tcgen05 GEMV over 51866 rows + exact fp16 rescoring + '
+                         'argmax + finalize)' if pruned else 'lm_head_kernel (final LN + fp16 GEMV + argmax)')}
+    blocks = {'self_block': (1, 0), 'cross_block': (1, 1), 'fc1': (1, 2), 'fc2': (1, 3), 'lm_head': (0, 4)}
+    table = {}
+    for key, (layer, block) in blocks.items():
+        if key == 'lm_head':
+            model.state.copy_(torch.tensor([length - 1, 0]))
+        us = graph_us(lambda: ext.decoder_launch(desc, layer, block))
+        gbs = nb[key] / (us * 1e-6) / 1e9
+        table[key] = {'kernel': names[key], 'us': round(us, 3), 'bytes': nb[key], 'gbs': round(gbs, 1),
+                      'frac': round(gbs / pk['hbm_gbs'], 4), 'launches_per_step': per_step[key],
+                      'ncu_traffic': NCU_TRAFFIC.get(key)}
+    total = sum(v['us'] * v['launches_per_step'] for v in table.values())
+    for v in table.values():
+        v['share'] = round(v['us'] * v['launches_per_step'] / total, 4)
+    model.state.zero_()
+    model.best.zero_()
+    torch.cuda.synchronize()
+    return table
+
+
+def micro_table(model, dims, pk):
+    """BASELINE configs 1 and 2 on this package's stand-alone kernels (inputs N(0,1) fp16 from seed 1,
+    logits N(0, 4) as std 2, ids U[0, vocab), positions 0..447; log-mel of seeded 30 s clips)."""
+    from flash_whisper_b200.audio import N_SAMPLES, synthetic_audio
+    from flash_whisper_b200.selftest import workspace
+    ext, dev, half = model.ext, 'cuda', torch.float16
+    g = torch.Generator(device=dev).manual_seed(1)
+    rn = lambda *s, std=1.0: (torch.randn(*s, generator=g, device=dev) * std).to(half)  # noqa: E731
+    d, heads, hd = dims.d_model, dims.heads, dims.head_dim
+    out = {}
+
+    def put(name, us, nbytes):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {'us': round(us, 3), 'bytes': int(nbytes), 'gbs': round(gbs, 1),
+                     'frac': round(gbs / pk['hbm_gbs'], 4)}
+
+    h, x, y = rn(d), rn(d), torch.empty(d, dtype=half, device=dev)
+    gamma, beta = rn(d), rn(d)
+    put('residual_layernorm', graph_us(lambda: ext.add_layernorm(h, x, gamma, beta, y, 1e-5), 100), 6 * d * 2)
+    xg, yg = rn(dims.ffn), torch.empty(dims.ffn, dtype=half, device=dev)
+    put('gelu_5120', graph_us(lambda: ext.gelu(xg, yg), 100), 2 * dims.ffn * 2)
+    ids = torch.randint(0, dims.vocab, (dims.max_pos,), generator=g, device=dev)
+    positions = torch.arange(dims.max_pos, device=dev)
+    emb_out = torch.empty(dims.max_pos, d, dtype=half, device=dev)
+    put('embed_gather_pos_448', graph_us(lambda: ext.embed_pos(model.dec.embed, model.dec.pos_embed, ids, positions,
+                                                               emb_out), 100), dims.max_pos * 3 * d * 2)
+    ws = workspace(heads, -(-dims.enc_len // 64), dev)
+    scale = hd ** -0.5
+    q, o = rn(heads * hd), torch.empty(heads * hd, dtype=half, device=dev)
+    k, v = rn(heads, dims.max_pos, hd), rn(heads, dims.max_pos, hd)
+    kn, vn = rn(heads, 1, hd), rn(heads, 1, hd)
+    for length in (1, 64, 224, 448):
+        st = torch.tensor([length - 1, 0], device=dev)
+        us = graph_us(lambda: ext.decode_attention(q, k, v, o, st, kn, vn, *ws, scale), 50)
+        put(f'self_attention_L{length}', us, 2 * heads * hd * 2 * length + 3 * heads * hd * 2)
+    kc, vc = rn(heads, dims.enc_len, hd), rn(heads, dims.enc_len, hd)
+    put('cross_attention_1500', graph_us(lambda: ext.decode_attention(q, kc, vc, o, None, None, None, *ws, scale),
+                                         50), 2 * heads * hd * 2 * dims.enc_len + 2 * heads * hd * 2)
+    logits = rn(dims.vocab, std=2.0)
+    key = torch.zeros(1, dtype=torch.long, device=dev)
+    idx = torch.zeros(1, dtype=torch.long, device=dev)
+    put('argmax_51866', graph_us(lambda: ext.argmax_f16(logits, None, key, idx), 100), dims.vocab * 2)
+    torch.cuda.synchronize()
+    out['argmax_51866']['matches_torch'] = int(idx) == int(torch.argmax(logits.float()))
+    for batch in (1, 32):
+        wave = torch.from_numpy(np.stack([synthetic_audio(s, SECONDS) for s in range(batch)])).to(dev)
+        assert wave.shape == (batch, N_SAMPLES)
+        scratch = torch.empty(batch, dims.n_mels, dims.n_frames, device=dev)
+        cmax = torch.zeros(batch, dtype=torch.int32, device=dev)
+        mel = torch.empty(batch, dims.n_mels, dims.n_frames, dtype=half, device=dev)
+        us = graph_us(lambda: ext.log_mel(wave, model.filters, scratch, cmax, mel, layout=0), 5 if batch > 1 else 20)
+        put(f'log_mel_batch{batch}', us, batch * (N_SAMPLES * 4 + dims.n_mels * dims.n_frames * 2))
+        out[f'log_mel_batch{batch}']['clips_per_s'] = round(batch / (us * 1e-6), 1)
+    torch.cuda.synchronize()
+    return out
+
+
+def config4(args, model, dims, ranks, rank, world, pk):
+    """the 256-clip stream, statically partitioned over the ranks, as batch-1
+    streams (one clip at a time through the graphed pipeline). Device time with the audio resident,
+    and end to end through transcribe() from host audio."""
+    from flash_whisper_b200.audio import synthetic_audio
+    clips = clip_set()
+    parts = partition(clips, world)
+    mine = parts[rank]
+    audios = {i: synthetic_audio(clips[i][0], clips[i][1]) for i in mine}
+    waves = torch.zeros(max(1, len(mine)), 480000, dtype=torch.float32, device='cuda')
+    for j, i in enumerate(mine):
+        waves[j, :audios[i].size] = torch.from_numpy(audios[i]).cuda()
+    stream = torch.cuda.current_stream()
+    for j, i in enumerate(mine[:3]):
+        model.wave.copy_(waves[j])
+        model.decode_device(clips[i][2])
+    torch.cuda.synchronize()
+    ranks.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for j, i in enumerate(mine):
+        model.wave.copy_(waves[j])
+        model.decode_device(clips[i][2])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    dev_ms = e0.elapsed_time(e1)
+    max_ms, min_ms = ranks.reduce(dev_ms, 'max'), ranks.reduce(dev_ms, 'min')
+    ranks.barrier()
+    t0 = time.perf_counter()
+    for i in mine:
+        model.transcribe(audios[i], max_new_tokens=clips[i][2], stop_at_eos=False)
+    e2e_s = ranks.reduce(time.perf_counter() - t0, 'max')
+    ranks.barrier()
+    total_audio = sum(c[1] for c in clips)
+    loads = [sum(clips[i][2] for i in p) for p in parts]
+    launches = sum(2 + (2 + 7 * dims.encoder_layers + 2) + (4 * dims.decoder_layers + 1) * (3 + clips[i][2])
+                   for i in mine)
+    return {
+        'workload': f'BASELINE config 4: {len(clips)} clips (seeds 0..{len(clips) - 1}, U[5,30] s from '
+                    'default_rng(0), padded to 30 s), round(7.5 tok/s x s) forced tokens, static longest-first '
+                    'partition over the ranks, batch-1 streams',
+        'audio_seconds': round(total_audio, 2), 'tokens': sum(c[2] for c in clips),
+        'whole_box_audio_s_per_s': round(total_audio / (max_ms / 1e3), 2),
+        'e2e_audio_s_per_s': round(total_audio / e2e_s, 2),
+        'max_rank_ms': round(max_ms, 3), 'min_rank_ms': round(min_ms, 3),
+        'tail_imbalance': round(max_ms / min_ms - 1.0, 4) if min_ms > 0 else None,
+        'rank_token_loads': {'max': max(loads), 'min': min(loads)},
+        'gpu_launches_rank0': launches,
+    }
 
 
 @torch.inference_mode()
@@ -218,6 +454,7 @@ def bench_ours(args, rank, world, local_rank):
     from flash_whisper_b200.weights import TURBO, random_state_dict
 
     torch.cuda.set_device(local_rank)
+    ranks = Ranks(world)
     dims = TURBO
     model = CustomModel(state_dict=random_state_dict(0, dims), dims=dims, selftest=False)
     audio = synthetic_audio(rank, SECONDS)
@@ -225,23 +462,12 @@ def bench_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
 
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-
-    def maxed(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device='cuda')
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t)
-
     for _ in range(args.warmup):
         model.decode_device(N_TOKENS)
     torch.cuda.synchronize()
 
     # (1) device time of a full step, inputs resident in HBM
-    barrier()
+    ranks.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
@@ -252,15 +478,15 @@ def bench_ours(args, rank, world, local_rank):
         e1.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
-    barrier()
-    step_ms = maxed(e0.elapsed_time(e1) / args.steps)
+    ranks.barrier()
+    step_ms = ranks.reduce(e0.elapsed_time(e1) / args.steps)
     toks = model.tokens[:N_TOKENS].tolist()
 
-    # (2) stage breakdown: mel, encoder, prompt, decode per token
+    # (2) stage breakdown: mel, encoder, prompt (yields the first token), decode per token
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     reps = max(3, args.steps)
-    mel_ms = enc_ms = dec_ms = 0.0
-    dec_steps = N_TOKENS - 1  # the prompt's last step yields the first token
+    mel_ms = enc_ms = prompt_ms = dec_ms = 0.0
+    dec_steps = N_TOKENS - 1
     for _ in range(reps):
         ev[0].record(stream)
         model.run_mel()
@@ -274,90 +500,86 @@ def bench_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         mel_ms += ev[0].elapsed_time(ev[1]) / reps
         enc_ms += ev[1].elapsed_time(ev[2]) / reps
+        prompt_ms += ev[2].elapsed_time(ev[3]) / reps
         dec_ms += ev[3].elapsed_time(ev[4]) / reps
-    us_per_token = maxed(dec_ms * 1e3 / dec_steps)
+    us_per_token = ranks.reduce(dec_ms * 1e3 / dec_steps)
 
-    # (3) LM-head kernel alone (the largest single kernel of the decode step), same stream, on the
-    # final-LayerNorm output of the last decoded step (the stand-alone entry takes x after the LN)
-    lm_iters = 50
-    ext = model.ext
-    best = torch.zeros(1, dtype=torch.long, device='cuda')
-    x_lm = torch.nn.functional.layer_norm(model.h.float(), (dims.d_model,), model.dec.final_ln[0].float(),
-                                          model.dec.final_ln[1].float(), dims.eps).half()
-
-    def lm_once():
-        if model.lm_q is not None:
-            ext.lm_head_argmax_q(x_lm, model.dec.lm_head, model.lm_q, model.lm_rp, model.base_mask, best)
-        else:
-            ext.lm_head_argmax(x_lm, model.dec.lm_head, model.base_mask, best)
-    for _ in range(3):
-        lm_once()
-        best.zero_()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(lm_iters):
-        lm_once()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    lm_us = e0.elapsed_time(e1) * 1e3 / lm_iters
-
-    # (4) end to end through the public API: pinned host audio -> host token ids
+    # (3) end to end through the public API: pinned host audio -> host token ids
     for _ in range(2):
         model.transcribe(audio, max_new_tokens=N_TOKENS, stop_at_eos=False)
-    barrier()
+    ranks.barrier()
     torch.cuda.synchronize()
+    ttfts = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
         out = model.transcribe(audio, max_new_tokens=N_TOKENS, stop_at_eos=False)
-    e2e_ms = maxed((time.perf_counter() - t0) * 1e3 / args.steps)
-    barrier()
+        ttfts.append(out['ttft_s'])
+    e2e_ms = ranks.reduce((time.perf_counter() - t0) * 1e3 / args.steps)
+    ttft_ms = ranks.reduce(statistics.median(ttfts) * 1e3)
+    ranks.barrier()
     assert out['token_ids'] == toks, 'public API and device path disagree'
 
+    # (4) each decode launch on its own, configs 1 and 2, config 4
     pk = peaks()
-    avg_len = 4 + N_TOKENS / 2
+    kernels = decode_kernel_table(model, dims, pk)
+    dominant = max(kernels, key=lambda k: kernels[k]['share'])
+    micro = micro_table(model, dims, pk) if rank == 0 else None
+    c4 = config4(args, model, dims, ranks, rank, world, pk)
+
+    avg_len = 4 + N_TOKENS // 2
     pruned = model.lm_q is not None
-    step_bytes = decode_bytes_per_token(dims, int(avg_len), pruned)
-    lm_bytes = (dims.vocab * (dims.d_model + 16) if pruned else dims.vocab * dims.d_model * 2) + dims.vocab + \
-        dims.d_model * 2
-    lm_gbs = lm_bytes / (lm_us * 1e-6) / 1e9
+    step_bytes = decode_bytes_per_token(dims, avg_len, pruned)
+    step_bytes_fp16 = decode_bytes_per_token(dims, avg_len, False)
     dec_gbs = step_bytes / (us_per_token * 1e-6) / 1e9
+
+    def roofline(key, source):
+        k = kernels[key]
+        return {'bound': 'hbm', 'kernel': k['kernel'], 'achieved': k['gbs'], 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
+                'frac': k['frac'], 'traffic': k['ncu_traffic'], 'peak_source': pk['source'], 'launch_us': k['us'],
+                'bytes_per_launch': k['bytes'], 'share_of_step': k['share'], 'timing': source}
+
+    timing_note = ('CUDA events around 10 replays of a graph holding 20 PDL-chained launches of this block alone, '
+                   'self-attention length 116 (the mean over the 224-token decode)')
     # our kernels per step: log-mel 2; encoder: 2 convs, 7 per layer, final LN, cross-K/V GEMM;
     # decoder: 4 per layer + LM head, for the 4 prompt steps and every generated step
     launches_per_step = 2 + (2 + 7 * dims.encoder_layers + 2) + (4 * dims.decoder_layers + 1) * (4 + dec_steps)
     line = {
-        'metric': 'batch-1 30s-clip E2E latency', 'value': round(step_ms, 4), 'unit': 'ms', 'n_gpus': world,
+        'metric': METRIC, 'value': round(step_ms, 4), 'unit': 'ms', 'n_gpus': world,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(step_ms, 4), 'higher_is_better': False,
         'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f16', 'data': 'synthetic',
-        'config': {'workload': 'BASELINE config 3: GPU log-mel + graphed 32-layer encoder + graphed 4-layer decoder, '
-                               '30 s clip, greedy forced to 224 tokens',
-                   'model': 'whisper-large-v3-turbo architecture, random-init seed 0 (fp16)', 'global_batch': world,
-                   'seq_len': N_TOKENS, 'parallelism': f'replicas{world}' if world > 1 else 'single',
-                   'l2': 'working set larger than L2 (282 MB per decode step, 1.26 GB encoder weights)'},
+        'config': dict(CONFIG3, parallelism=f'replicas{world}' if world > 1 else 'single'),
         'e2e': {'value': round(e2e_ms, 4), 'unit': 'ms', 'h2d_bytes_per_step': 480000 * 4,
                 'd2h_bytes_per_step': N_TOKENS * 8},
+        'ttft_ms': round(ttft_ms, 4),
         'decode_us_per_token': round(us_per_token, 3),
-        'stages_ms': {'mel': round(mel_ms, 4), 'encoder': round(enc_ms, 4), 'decode': round(dec_ms, 4)},
+        'stages_ms': {'mel': round(mel_ms, 4), 'encoder': round(enc_ms, 4), 'prompt': round(prompt_ms, 4),
+                      'decode': round(dec_ms, 4)},
         'throughput_audio_s_per_s': round(world * SECONDS / (step_ms / 1e3), 2),
-        'roofline': {'bound': 'hbm', 'kernel': ('lm_head_q (int8 GEMV 51866x1280 with per-row bounds, exact fp16 '
-                                                'rescoring of the rows that can win, argmax)' if pruned else
-                                                'lm_head_argmax (GEMV 51866x1280 + argmax)'),
-                     'achieved': round(lm_gbs, 1), 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
-                     'frac': round(lm_gbs / pk['hbm_gbs'], 4), 'traffic': LM_HEAD_TRAFFIC_BYTES, 'peak_source': pk['source'],
-                     'launch_us': round(lm_us, 3), 'bytes_per_launch': lm_bytes},
-        'roofline_decode_step': {'bound': 'hbm', 'achieved': round(dec_gbs, 1), 'peak': pk['hbm_gbs'],
-                                 'unit': 'GB/s', 'frac': round(dec_gbs / pk['hbm_gbs'], 4),
-                                 'bytes_per_token': step_bytes},
+        'roofline': roofline(dominant, timing_note),
+        'roofline_lm_head': roofline('lm_head', timing_note),
+        'decode_kernels': kernels,
+        'roofline_decode_step': {
+            'bound': 'hbm', 'peak': pk['hbm_gbs'], 'unit': 'GB/s', 'self_attention_length': avg_len,
+            'int8_lm_head': {'bytes_per_token': step_bytes, 'achieved': round(dec_gbs, 1),
+                             'frac': round(dec_gbs / pk['hbm_gbs'], 4)},
+            'fp16_lm_head_equivalent': {'bytes_per_token': step_bytes_fp16,
+                                        'achieved': round(step_bytes_fp16 / (us_per_token * 1e-6) / 1e9, 1),
+                                        'frac': round(step_bytes_fp16 / (us_per_token * 1e-6) / 1e9 / pk['hbm_gbs'],
+                                                      4)}},
+        'config4': c4,
         'gpu_launches': launches_per_step * args.steps,
         'clocks': clocks.summary(),
     }
+    if micro is not None:
+        line['micro'] = micro
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu_model, cpu_audio = cpu_reference_sample(threads=host_threads())
-            v, t = run_cpu_sample(cpu_model, cpu_audio, 8)
-            line['cpu_baseline'] = {
-                'value': round(v, 3), 'unit': 'ms', 'cores': torch.get_num_threads(), 'kind': 'port',
-                'sample': 'CPU fp32 log-mel + encoder of one 30 s clip + 8 decode steps (oracle/hf_cpu.py, the '
-                          'custom/pytorch_model.py loop), E2E extrapolated to 224 tokens'}
+            threads = host_threads()
+            cpu_model, cpu_audio = cpu_reference_model(threads)
+            vals = [run_cpu_step(cpu_model, cpu_audio)[0] for _ in range(3)]
+            line['cpu_baseline'] = {'value': round(statistics.median(vals), 3), 'unit': 'ms',
+                                    'cores': torch.get_num_threads(), 'kind': 'port',
+                                    'sample': f'3 {CPU_SAMPLE}; median'}
         except Exception as exc:  # the baseline is reported, never required
             line['cpu_baseline'] = {'value': None, 'unit': 'ms', 'error': f'{type(exc).__name__}: {exc}'}
     if rank == 0:
@@ -365,101 +587,106 @@ def bench_ours(args, rank, world, local_rank):
     return 0
 
 
+# ---- reference CUDA backend A/B (run by hand) ---------------------------------------------------
 @torch.inference_mode()
-def bench_clips(args, rank, world, local_rank):
-    """the 256-clip stream, statically partitioned over the ranks."""
+def bench_refcuda(args):
+    """The reference's CUDA backend (oracle/ref_pipeline.py) and this package on the same GPU, weights
+    and audio: E2E, TTFT, encoder and per-token decode, token identity; then the reference kernels
+    (oracle/_ref) beside this package's on the config-1 microbench inputs."""
+    from flash_whisper_b200.audio import synthetic_audio
+    from flash_whisper_b200.model import CustomModel
+    from flash_whisper_b200.selftest import workspace
+    from flash_whisper_b200.weights import TURBO, random_state_dict
+    from oracle.build_ref import load_ref
+    from oracle.ref_pipeline import RefCudaBackend
+
+    dims = TURBO
+    sd = random_state_dict(0, dims)
+    audio = synthetic_audio(0, SECONDS)
+    out = {'workload': 'refcuda', 'config': dict(CONFIG3, parallelism='single')}
+    with ClockSampler(0) as clocks:
+        ref = RefCudaBackend(sd, dims)
+        for _ in range(args.warmup):
+            ref.transcribe(audio, N_TOKENS)
+        runs = [ref.transcribe(audio, N_TOKENS) for _ in range(args.steps)]
+        ref_tokens = runs[0][0]
+        med = lambda k: statistics.median(r[1][k] for r in runs) * 1e3  # noqa: E731
+        ref_tok_us = replay_us(ref.graph_chunk.replay) / 8
+        out['reference_cuda_backend'] = {'e2e_ms': round(med('e2e_s'), 3), 'ttft_ms': round(med('ttft_s'), 3),
+                                         'mel_ms': round(med('mel_s'), 3), 'encoder_ms': round(med('encoder_s'), 3),
+                                         'decode_us_per_token': round(ref_tok_us, 2)}
+        del ref
+        torch.cuda.empty_cache()
+        model = CustomModel(state_dict=sd, dims=dims, selftest=False)
+        for _ in range(args.warmup):
+            model.transcribe(audio, max_new_tokens=N_TOKENS, stop_at_eos=False)
+        outs = [model.transcribe(audio, max_new_tokens=N_TOKENS, stop_at_eos=False) for _ in range(args.steps)]
+        ours_tok_us = replay_us(model.run_chunk) / model.chunk
+        medo = lambda k: statistics.median(o[k] for o in outs) * 1e3  # noqa: E731
+        out['flash_whisper_b200'] = {'e2e_ms': round(medo('e2e_s'), 3), 'ttft_ms': round(medo('ttft_s'), 3),
+                                     'mel_ms': round(medo('mel_s'), 3), 'encoder_ms': round(medo('encoder_s'), 3),
+                                     'decode_us_per_token': round(ours_tok_us, 2)}
+        out['token_ids_identical'] = outs[0]['token_ids'] == ref_tokens[:N_TOKENS]
+        # reference kernels vs this package's, config-1 inputs
+        refk, ext = load_ref(), model.ext
+        dev, half = 'cuda', torch.float16
+        g = torch.Generator(device=dev).manual_seed(1)
+        rn = lambda *s, std=1.0: (torch.randn(*s, generator=g, device=dev) * std).to(half)  # noqa: E731
+        heads, hd, d = dims.heads, dims.head_dim, dims.d_model
+        ws = workspace(heads, -(-dims.enc_len // 64), dev)
+        scale = hd ** -0.5
+        micro = {}
+        h, x, y = rn(1, d), rn(1, d), torch.empty(1, d, dtype=half, device=dev)
+        gm, bt = rn(d), rn(d)
+        micro['residual_layernorm'] = (graph_us(lambda: refk.add_layernorm(h, x, gm, bt, y, 1e-5), 100),
+                                       graph_us(lambda: ext.add_layernorm(h, x, gm, bt, y, 1e-5), 100))
+        q, o = rn(heads, 1, hd), torch.empty(heads * hd, dtype=half, device=dev)
+        k, v = rn(heads, dims.max_pos, hd), rn(heads, dims.max_pos, hd)
+        kn, vn = rn(heads, 1, hd), rn(heads, 1, hd)
+        for length in (1, 64, 224, 448):
+            st = torch.tensor([length - 1, 0], device=dev)
+            micro[f'self_attention_L{length}'] = (
+                graph_us(lambda: refk.decode_attention(q, k, v, o, st, kn, vn, *ws, scale), 50),
+                graph_us(lambda: ext.decode_attention(q.view(-1), k, v, o, st, kn, vn, *ws, scale), 50))
+        kc, vc = rn(heads, dims.enc_len, hd), rn(heads, dims.enc_len, hd)
+        micro['cross_attention_1500'] = (
+            graph_us(lambda: refk.decode_attention(q, kc, vc, o, None, None, None, *ws, scale), 50),
+            graph_us(lambda: ext.decode_attention(q.view(-1), kc, vc, o, None, None, None, *ws, scale), 50))
+        yl = rn(1, d)
+        sup = torch.zeros(dims.vocab, dtype=torch.bool, device=dev)
+        best = torch.zeros(1, dtype=torch.long, device=dev)
+
+        def ref_lm():
+            refk.lm_head_argmax(yl, model.dec.lm_head, sup, best)
+            best.zero_()
+
+        def our_lm():
+            ext.lm_head_argmax(yl, model.dec.lm_head, sup, best)
+            best.zero_()
+
+        micro['lm_head_argmax_fp16'] = (graph_us(ref_lm, 20), graph_us(our_lm, 20))
+        out['kernels_us_reference_vs_ours'] = {k: [round(a, 3), round(b, 3)] for k, (a, b) in micro.items()}
+    out['clocks'] = clocks.summary()
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+@torch.inference_mode()
+def profile_run(args):
+    """Eager run of one transcription (log-mel, encoder, prompt, `--tokens` decode steps), one launch
+    after another, so a profiler can select single launches by kernel name and index."""
     from flash_whisper_b200.audio import synthetic_audio
     from flash_whisper_b200.model import CustomModel
     from flash_whisper_b200.weights import TURBO, random_state_dict
-
-    torch.cuda.set_device(local_rank)
-    dims = TURBO
-    model = CustomModel(state_dict=random_state_dict(0, dims), dims=dims, selftest=False)
-    clips = clip_set()
-    mine = partition(clips, world)[rank]
-    audios = {i: synthetic_audio(clips[i][0], clips[i][1]) for i in mine}
-    waves = torch.zeros(max(1, len(mine)), 480000, dtype=torch.float32, device='cuda')  # resident in HBM
-    for j, i in enumerate(mine):
-        waves[j, :audios[i].size] = torch.from_numpy(audios[i]).cuda()
-    stream = torch.cuda.current_stream()
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-
-    def reduce(x, op):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device='cuda')
-        torch.distributed.all_reduce(t, op=op)
-        return float(t)
-
-    for j, i in enumerate(mine[:max(args.warmup, 3)]):
-        model.wave.copy_(waves[j])
-        model.decode_device(clips[i][2])
+    model = CustomModel(state_dict=random_state_dict(0, TURBO), dims=TURBO, selftest=False, capture=False)
+    model.load_audio(synthetic_audio(0, SECONDS))
+    model._mel()
+    model._encode()
+    model._prompt()
+    for _ in range(args.tokens):
+        model.ext.decoder_step(model.dec_desc, 1)
     torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        e0.record(stream)
-        for j, i in enumerate(mine):
-            model.wave.copy_(waves[j])
-            model.decode_device(clips[i][2])
-        e1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    max_ms = reduce(e0.elapsed_time(e1), torch.distributed.ReduceOp.MAX if world > 1 else None)
-    total_audio = sum(c[1] for c in clips)
-    total_tokens = sum(c[2] for c in clips)
-    launches = reduce(sum(2 + (2 + 7 * dims.encoder_layers + 2) + (4 * dims.decoder_layers + 1) * (3 + clips[i][2])
-                          for i in mine), torch.distributed.ReduceOp.SUM if world > 1 else None)
-
-    # end to end through the public API: host audio -> host token ids, same partition
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for i in mine:
-        model.transcribe(audios[i], max_new_tokens=clips[i][2], stop_at_eos=False)
-    e2e_s = reduce(time.perf_counter() - t0, torch.distributed.ReduceOp.MAX if world > 1 else None)
-    barrier()
-
-    value = total_audio / (max_ms / 1e3)
-    avg_len = 4 + total_tokens / len(clips) / 2
-    dec_bytes = decode_bytes_per_token(dims, int(avg_len))
-    line = {
-        'metric': 'whole-box stream throughput (BASELINE config 4)', 'value': round(value, 2), 'unit': 'audio-s/s',
-        'n_gpus': world, 'steps': 1, 'warmup': args.warmup, 'ms_per_step': round(max_ms, 3),
-        'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f16', 'data': 'synthetic',
-        'config': {'workload': f'BASELINE config 4: {len(clips)} clips (audio seeds 0..{len(clips) - 1}, U[5,30] s '
-                               f'lengths from default_rng(0), padded to 30 s), round(7.5 tokens/s x s) forced tokens; '
-                               'static longest-first partition over ranks; one step = the whole set',
-                   'model': 'whisper-large-v3-turbo architecture, random-init seed 0 (fp16)', 'clips': len(clips),
-                   'audio_seconds': round(total_audio, 2), 'tokens': total_tokens,
-                   'parallelism': f'replicas{world}' if world > 1 else 'single',
-                   'l2': 'working set larger than L2 (282 MB per decode step, 1.26 GB encoder weights)'},
-        'e2e': {'value': round(total_audio / e2e_s, 2), 'unit': 'audio-s/s',
-                'h2d_bytes_per_step': len(clips) * 480000 * 4, 'd2h_bytes_per_step': total_tokens * 8},
-        'rank0_clips': len(mine),
-        'roofline_decode_step': {'bound': 'hbm', 'bytes_per_token': dec_bytes,
-                                 'note': 'per-token decode bytes at the mean self-attention length'},
-        'gpu_launches': int(launches),
-        'clocks': clocks.summary(),
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            cpu_model, cpu_audio = cpu_reference_sample(threads=host_threads())
-            _, t = run_cpu_sample(cpu_model, cpu_audio, 8)
-            per_tok = t['decode_s'] / max(1, t['n_tokens'])
-            cpu_s = len(clips) * (t['mel_s'] + t['encoder_s']) + total_tokens * per_tok
-            line['cpu_baseline'] = {
-                'value': round(total_audio / cpu_s, 3), 'unit': 'audio-s/s', 'cores': torch.get_num_threads(),
-                'kind': 'port', 'sample': 'CPU fp32 log-mel + encoder of one 30 s clip + 8 decode steps (oracle/hf_cpu.py), '
-                                          'extrapolated to the 256 clips and their forced tokens'}
-        except Exception as exc:  # the baseline is reported, never required
-            line['cpu_baseline'] = {'value': None, 'unit': 'audio-s/s', 'error': f'{type(exc).__name__}: {exc}'}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    print('tokens', model.tokens[:args.tokens + 1].tolist())
     return 0
 
 
@@ -470,21 +697,21 @@ def main():
     parser.add_argument('--warmup', type=int, default=3)
     parser.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     parser.add_argument('--no-cpu-baseline', action='store_true')
-    parser.add_argument('--workload', choices=('clip30', 'clips256'), default='clip30')
+    parser.add_argument('--workload', choices=('clip30', 'refcuda', 'profile'), default='clip30')
+    parser.add_argument('--tokens', type=int, default=4, help='decode steps of --workload profile')
     args = parser.parse_args()
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local_rank = int(os.environ.get('LOCAL_RANK', '0'))
     if args.impl == 'reference':
         return bench_reference(args, rank, world)
+    if args.workload == 'refcuda':
+        return bench_refcuda(args) if rank == 0 else 0
+    if args.workload == 'profile':
+        return profile_run(args)
     if world > 1:
-        import datetime
-        torch.cuda.set_device(local_rank)
-        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=600),
-                                             device_id=torch.device('cuda', local_rank))
+        torch.distributed.init_process_group('gloo', timeout=datetime.timedelta(seconds=300))
     try:
-        if args.workload == 'clips256':
-            return bench_clips(args, rank, world, local_rank)
         return bench_ours(args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -17,6 +17,9 @@ HEADER = PKG.parent / 'include' / 'flash_whisper.h'
 FW_OK = 0
 FW_EPI_BIAS, FW_EPI_BIAS_GELU, FW_EPI_BIAS_RESID, FW_EPI_GELU_POS, FW_EPI_CROSS_KV, FW_EPI_BIAS_SCALE, FW_EPI_QKV_VT = range(7)
 MAX_LAYERS = 8
+# fw_decoder_step_trace buffer layout (fp16 element offsets within one layer's record)
+TRACE_SELF_ATTN, TRACE_H_SELF, TRACE_CROSS_ATTN, TRACE_H_CROSS, TRACE_FFN, TRACE_H_FFN = 0, 1280, 2560, 3840, 5120, 10240
+TRACE_LAYER = 11520
 MAX_ENC_LAYERS = 32
 
 vp = c_void_p
@@ -79,6 +82,8 @@ _SIGNATURES = {
     'fw_ln_gemv': (c_int, [vp, vp, vp, c_float, vp, vp, vp, c_int, c_int, c_int, vp]),
     'fw_gemv_residual': (c_int, [vp, c_int, vp, vp, vp, c_int, vp]),
     'fw_decoder_step': (c_int, [POINTER(Decoder), c_int, vp]),
+    'fw_decoder_step_trace': (c_int, [POINTER(Decoder), vp, vp]),
+    'fw_decoder_launch': (c_int, [POINTER(Decoder), c_int, c_int, vp]),
     'fw_log_mel': (c_int, [vp, c_int, c_int, vp, vp, vp, vp, c_int, vp]),
     'fw_gemm_f16': (c_int, [vp, c_int64, vp, c_int64, vp, vp, c_int64, vp, c_int64, c_int, c_int, c_int, c_int,
                             c_float, c_int, vp]),

@@ -869,6 +869,7 @@ struct LmParams {
   int64_t* cur;
   int max_pos;
   int prompt_len;
+  half* y_out;  // optional [1280]: CTA 0 writes the (LayerNorm) input row it dotted (fw_decoder_step_trace)
 };
 
 // Token bookkeeping shared by argmax_finalize and the fused LM-head tail.
@@ -952,6 +953,10 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
     for (int i = 0; i < 5; ++i) ys[threadIdx.x + i * 256] = p.h[threadIdx.x + i * 256];
   }
   __syncthreads();
+  if (p.y_out && blockIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) p.y_out[threadIdx.x + i * 256] = ys[threadIdx.x + i * 256];
+  }
   float xf[40];
   load_x40(ys, xf);
 
@@ -1014,8 +1019,11 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
 //   a_r  = max_i |w_ri - s_r q_ri| + 1e-5 max_i |w_ri|
 //   c2_r = 0.51 s_r sum_i |q_ri|
 // The kernel quantises the LayerNorm output x to 14-bit integers xq (scale sx = max|x| / 8191, so
-// |x_i - sx xq_i| <= 0.51 sx), streams q, and forms the exact integer S_r = sum_i xq_i q_ri with
-// dp2a. approx_r = s_r sx S_r then satisfies |dot_r - approx_r| <= B_r with
+// |x_i - sx xq_i| <= 0.51 sx), splits them as xq = 128 x_hi + x_lo with x_hi in [-64, 64] and x_lo in
+// [-64, 63] (both int8), streams q, and forms the exact integer S_r = sum_i xq_i q_ri = 128 v0 + v1
+// from the two int32 columns v0 = sum_i q_ri x_hi_i and v1 = sum_i q_ri x_lo_i of a tcgen05.mma
+// kind::i8 against B = [x_hi; x_lo]. The int32 accumulators cannot overflow: |v0|, |v1| <= 1280 * 127
+// * 64 < 2^31, and |S_r| <= 1280 * 127 * 8191 < 2^31. approx_r = s_r sx S_r then satisfies |dot_r - approx_r| <= B_r with
 //   B_r = (|x|_1 a_r + sx c2_r + 4e-7 |approx_r|) (1 + 1e-5),
 // where dot_r is the fp32 value the exact kernel computes (its own rounding error is at most
 // 45 * 2^-24 |x|_1 max|w_r|, inside the 1e-5 term; the other terms bound the two quantisations
@@ -1205,6 +1213,10 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
       ys[threadIdx.x + i * 256] = y;
       xv[i] = __half2float(y);
     }
+  }
+  if (p.y_out && blockIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) p.y_out[threadIdx.x + i * 256] = __float2half(xv[i]);
   }
   // max|x| and |x|_1 of the fp16 LayerNorm output
   {
@@ -1865,11 +1877,31 @@ static int launch_lm_head_q(LmParams p, cudaStream_t s, bool pdl) {
 constexpr int kNoAllocMaxSlots = 2048;  // heads * ceil(max_len / 64)
 static __device__ __align__(256) float g_attn_noalloc_scratch[kNoAllocMaxSlots * (kHeadDim + 2)];
 
-// Device address of g_attn_noalloc_scratch on the current device; looked up on the first call per
-// device and cached. Returns nullptr and sets the error message on failure.
+// Device address of g_attn_noalloc_scratch in the current device's current context. The address is
+// looked up on the first call per device and cached together with the context it belongs to; a call
+// made in another context of that device (after cudaDeviceReset, or a primary context that was
+// released and re-created) looks it up again, since a new context loads the module afresh. Returns
+// nullptr and sets the error message on failure.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  CUcontext ctx = nullptr;
+  if (fn != nullptr && fn(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  return ctx;
+}
+
 static float* noalloc_scratch() {
   static std::mutex mu;
   static float* cached[64] = {nullptr};
+  static CUcontext cached_ctx[64] = {nullptr};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -1881,7 +1913,8 @@ static float* noalloc_scratch() {
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(mu);
-  if (cached[dev] == nullptr) {
+  const CUcontext ctx = current_context();
+  if (cached[dev] == nullptr || ctx == nullptr || ctx != cached_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -1889,6 +1922,7 @@ static float* noalloc_scratch() {
       return nullptr;
     }
     cached[dev] = static_cast<float*>(p);
+    cached_ctx[dev] = current_context();  // the lookup made the device's primary context current
   }
   return cached[dev];
 }
@@ -1954,7 +1988,7 @@ int fw_decode_attention_noalloc(const void* q, void* k, void* v, void* out, cons
   FW_REQUIRE((k_new != nullptr) == (v_new != nullptr) && (k_new != nullptr) == (len_state != nullptr), FW_ERR_ARG,
              "len_state, k_new and v_new must be given together");
   FW_REQUIRE(heads > 0 && max_len > 0, FW_ERR_SHAPE, "k, v must be [heads, max_len, 64]");
-  FW_REQUIRE(max_len <= kMaxSplits * kSplitKeys, FW_ERR_SHAPE, "decode_attention: max_len must be <= %d",
+  FW_REQUIRE(max_len <= kMaxSplits * kSplitKeys, FW_ERR_SHAPE, "decode_attention_noalloc: max_len must be <= %d",
              kMaxSplits * kSplitKeys);
   const int splits = (max_len + kSplitKeys - 1) / kSplitKeys;
   FW_REQUIRE(int64_t(heads) * splits <= kNoAllocMaxSlots, FW_ERR_SHAPE,
@@ -2111,7 +2145,12 @@ int fw_gemv_residual(const void* x, int k, const void* w, const void* b, void* h
   return launch_gemv_residual(p, static_cast<cudaStream_t>(stream), false);
 }
 
-int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
+}  // extern "C"
+
+namespace fw {
+
+// Checks a decoder descriptor (shared by fw_decoder_step and fw_decoder_step_trace).
+static int check_decoder(const fw_decoder_t* d) {
   FW_REQUIRE(d != nullptr, FW_ERR_NULL, "decoder_step: descriptor is NULL");
   FW_REQUIRE(d->n_layers > 0 && d->n_layers <= FW_MAX_LAYERS, FW_ERR_SHAPE, "decoder_step: bad layer count");
   FW_REQUIRE(d->heads * kHeadDim == kHidden, FW_ERR_SHAPE, "decoder_step: heads * 64 must be %d", kHidden);
@@ -2130,86 +2169,17 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
              kHeadCtas * kHeadMaxUnits * kSplitKeys);
   FW_REQUIRE(d->ws_splits * kHeadDim >= kHidden, FW_ERR_SHAPE,
              "decoder_step: part_acc must hold heads * 1280 floats (ws_splits >= %d)", kHidden / kHeadDim);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (steps <= 0) return FW_OK;
+  return FW_OK;
+}
+
+// Launch `block` of layer `l` of the decode step: 0 self-attention block, 1 cross-attention block,
+// 2 LN3 + fc1 + GELU, 3 fc2 + residual; block 4 (l ignored) is the LM head with the final LayerNorm,
+// argmax and token bookkeeping. `tl` (this layer's trace record) and `y_out` are optional outputs of
+// fw_decoder_step_trace.
+static int decoder_launch(const fw_decoder_t* d, int l, int block, cudaStream_t s, half* tl, half* y_out) {
   half* h = static_cast<half*>(d->h);
   half* ffn = static_cast<half*>(d->ffn);
-  for (int step = 0; step < steps; ++step) {
-    for (int l = 0; l < d->n_layers; ++l) {
-      const fw_decoder_layer_t& L = d->layers[l];
-      int rc;
-      // LN1 + q/k/v (+ embedding on layer 0) + self attention with the cache write + out_proj + residual
-      HeadBlockParams a{};
-      a.h = h;
-      a.gamma = static_cast<const half*>(L.ln1_g);
-      a.beta = static_cast<const half*>(L.ln1_b);
-      a.eps = d->eps;
-      a.embed = static_cast<const half*>(d->embed);
-      a.pos_embed = static_cast<const half*>(d->pos_embed);
-      a.cur = d->cur;
-      a.prompt = d->prompt;
-      a.prompt_len = d->prompt_len;
-      a.vocab = d->vocab;
-      a.state = d->state;
-      a.max_pos = d->max_pos;
-      a.state_early = l > 0;  // on layer 0 the previous launch (LM head) advances the position
-      a.w = static_cast<const half*>(L.qkv_w);
-      a.b = static_cast<const half*>(L.qkv_b);
-      a.k = static_cast<half*>(L.self_k);
-      a.v = static_cast<half*>(L.self_v);
-      a.kv_len = d->max_pos;
-      a.scale = d->scale;
-      a.wo = static_cast<const half*>(L.out_w);
-      a.bo = static_cast<const half*>(L.out_b);
-      a.part = d->part_acc;
-      a.counter = d->counters;
-      a.attn_out = static_cast<half*>(d->attn);
-      rc = l == 0 ? launch_head_block<true, true>(a, d->heads, s, true)
-                  : launch_head_block<true, false>(a, d->heads, s, true);
-      if (rc) return rc;
-      // LN2 + cross q + cross attention + cross out_proj + residual
-      HeadBlockParams c{};
-      c.h = h;
-      c.gamma = static_cast<const half*>(L.ln2_g);
-      c.beta = static_cast<const half*>(L.ln2_b);
-      c.eps = d->eps;
-      c.state = d->state;
-      c.max_pos = d->max_pos;
-      c.w = static_cast<const half*>(L.cq_w);
-      c.b = static_cast<const half*>(L.cq_b);
-      c.k = const_cast<half*>(static_cast<const half*>(L.cross_k));
-      c.v = const_cast<half*>(static_cast<const half*>(L.cross_v));
-      c.kv_len = d->enc_len;
-      c.scale = d->scale;
-      c.wo = static_cast<const half*>(L.co_w);
-      c.bo = static_cast<const half*>(L.co_b);
-      c.part = d->part_acc;
-      c.counter = d->counters;
-      if ((rc = launch_head_block<false, false>(c, d->heads, s, true))) return rc;
-      // LN3 + fc1 + GELU
-      GemvParams g{};
-      g.w = static_cast<const half*>(L.fc1_w);
-      g.b = static_cast<const half*>(L.fc1_b);
-      g.out = ffn;
-      g.n_out = kFfn;
-      g.k = kHidden;
-      g.rows_per_cta = kFc1Rows;
-      g.h = h;
-      g.gamma = static_cast<const half*>(L.ln3_g);
-      g.beta = static_cast<const half*>(L.ln3_b);
-      g.eps = d->eps;
-      if ((rc = launch_ln_gemv<1>(g, s, true))) return rc;
-      // fc2 + residual
-      GemvParams r{};
-      r.w = static_cast<const half*>(L.fc2_w);
-      r.b = static_cast<const half*>(L.fc2_b);
-      r.n_out = kHidden;
-      r.k = kFfn;
-      r.rows_per_cta = kResidRows;
-      r.x = ffn;
-      r.h_res = h;
-      if ((rc = launch_gemv_residual(r, s, true))) return rc;
-    }
+  if (block == 4) {
     LmParams m{};
     m.h = h;
     m.gamma = static_cast<const half*>(d->final_g);
@@ -2227,17 +2197,144 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
     m.cur = d->cur;
     m.max_pos = d->max_pos;
     m.prompt_len = d->prompt_len;
-    int rc;
+    m.y_out = y_out;
     if (d->lm_q != nullptr) {
       m.wq = static_cast<const int8_t*>(d->lm_q);
       m.rp = static_cast<const float4*>(d->lm_rp);
-      rc = launch_lm_head_q<true, true>(m, s, true);
-    } else {
-      rc = launch_lm_head<true, true>(m, s, true);
+      return launch_lm_head_q<true, true>(m, s, true);
     }
-    if (rc) return rc;
+    return launch_lm_head<true, true>(m, s, true);
   }
+  const fw_decoder_layer_t& L = d->layers[l];
+  if (block == 0) {
+    // LN1 + q/k/v (+ embedding on layer 0) + self attention with the cache write + out_proj + residual
+    HeadBlockParams a{};
+    a.h = h;
+    a.gamma = static_cast<const half*>(L.ln1_g);
+    a.beta = static_cast<const half*>(L.ln1_b);
+    a.eps = d->eps;
+    a.embed = static_cast<const half*>(d->embed);
+    a.pos_embed = static_cast<const half*>(d->pos_embed);
+    a.cur = d->cur;
+    a.prompt = d->prompt;
+    a.prompt_len = d->prompt_len;
+    a.vocab = d->vocab;
+    a.state = d->state;
+    a.max_pos = d->max_pos;
+    a.state_early = l > 0;  // on layer 0 the previous launch (LM head) advances the position
+    a.w = static_cast<const half*>(L.qkv_w);
+    a.b = static_cast<const half*>(L.qkv_b);
+    a.k = static_cast<half*>(L.self_k);
+    a.v = static_cast<half*>(L.self_v);
+    a.kv_len = d->max_pos;
+    a.scale = d->scale;
+    a.wo = static_cast<const half*>(L.out_w);
+    a.bo = static_cast<const half*>(L.out_b);
+    a.part = d->part_acc;
+    a.counter = d->counters;
+    a.attn_out = tl ? tl + FW_TRACE_SELF_ATTN : static_cast<half*>(d->attn);
+    return l == 0 ? launch_head_block<true, true>(a, d->heads, s, true)
+                  : launch_head_block<true, false>(a, d->heads, s, true);
+  }
+  if (block == 1) {
+    // LN2 + cross q + cross attention + cross out_proj + residual
+    HeadBlockParams c{};
+    c.h = h;
+    c.gamma = static_cast<const half*>(L.ln2_g);
+    c.beta = static_cast<const half*>(L.ln2_b);
+    c.eps = d->eps;
+    c.state = d->state;
+    c.max_pos = d->max_pos;
+    c.w = static_cast<const half*>(L.cq_w);
+    c.b = static_cast<const half*>(L.cq_b);
+    c.k = const_cast<half*>(static_cast<const half*>(L.cross_k));
+    c.v = const_cast<half*>(static_cast<const half*>(L.cross_v));
+    c.kv_len = d->enc_len;
+    c.scale = d->scale;
+    c.wo = static_cast<const half*>(L.co_w);
+    c.bo = static_cast<const half*>(L.co_b);
+    c.part = d->part_acc;
+    c.counter = d->counters;
+    c.attn_out = tl ? tl + FW_TRACE_CROSS_ATTN : nullptr;
+    return launch_head_block<false, false>(c, d->heads, s, true);
+  }
+  if (block == 2) {
+    // LN3 + fc1 + GELU
+    GemvParams g{};
+    g.w = static_cast<const half*>(L.fc1_w);
+    g.b = static_cast<const half*>(L.fc1_b);
+    g.out = ffn;
+    g.n_out = kFfn;
+    g.k = kHidden;
+    g.rows_per_cta = kFc1Rows;
+    g.h = h;
+    g.gamma = static_cast<const half*>(L.ln3_g);
+    g.beta = static_cast<const half*>(L.ln3_b);
+    g.eps = d->eps;
+    return launch_ln_gemv<1>(g, s, true);
+  }
+  // fc2 + residual
+  GemvParams r{};
+  r.w = static_cast<const half*>(L.fc2_w);
+  r.b = static_cast<const half*>(L.fc2_b);
+  r.n_out = kHidden;
+  r.k = kFfn;
+  r.rows_per_cta = kResidRows;
+  r.x = ffn;
+  r.h_res = h;
+  return launch_gemv_residual(r, s, true);
+}
+
+// One decode step: 4 launches per layer and the LM head. With `trace` set (fw_decoder_step_trace),
+// the same launches also leave each block's output in `trace` (FW_TRACE_* layout): the attention
+// outputs and the final LayerNorm row are written by the kernels themselves, the residual stream and
+// the fc1 output are copied after the launch that produced them.
+static int decoder_one_step(const fw_decoder_t* d, cudaStream_t s, half* trace) {
+  half* h = static_cast<half*>(d->h);
+  auto snap = [&](half* dst, const void* src, int n) -> int {
+    cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(n) * sizeof(half), cudaMemcpyDeviceToDevice, s);
+    return e == cudaSuccess ? FW_OK : set_error(FW_ERR_LAUNCH, "decoder_step_trace: copy: %s", cudaGetErrorString(e));
+  };
+  static const int kSnapAt[4] = {FW_TRACE_H_SELF, FW_TRACE_H_CROSS, FW_TRACE_FFN, FW_TRACE_H_FFN};
+  for (int l = 0; l < d->n_layers; ++l) {
+    half* tl = trace ? trace + static_cast<size_t>(l) * FW_TRACE_LAYER : nullptr;
+    for (int block = 0; block < 4; ++block) {
+      int rc = decoder_launch(d, l, block, s, tl, nullptr);
+      if (rc) return rc;
+      if (tl && (rc = snap(tl + kSnapAt[block], block == 2 ? d->ffn : h, block == 2 ? kFfn : kHidden))) return rc;
+    }
+  }
+  return decoder_launch(d, 0, 4, s, nullptr,
+                        trace ? trace + static_cast<size_t>(d->n_layers) * FW_TRACE_LAYER : nullptr);
+}
+
+}  // namespace fw
+
+extern "C" {
+
+int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream) {
+  int rc = check_decoder(d);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int step = 0; step < steps; ++step)
+    if ((rc = decoder_one_step(d, s, nullptr))) return rc;
   return FW_OK;
+}
+
+int fw_decoder_launch(const fw_decoder_t* d, int layer, int block, fw_stream_t stream) {
+  int rc = check_decoder(d);
+  if (rc) return rc;
+  FW_REQUIRE(block >= 0 && block <= 4, FW_ERR_ARG, "decoder_launch: block must be 0..4");
+  FW_REQUIRE(block == 4 || (layer >= 0 && layer < d->n_layers), FW_ERR_ARG, "decoder_launch: layer out of range");
+  return decoder_launch(d, block == 4 ? 0 : layer, block, static_cast<cudaStream_t>(stream), nullptr, nullptr);
+}
+
+int fw_decoder_step_trace(const fw_decoder_t* d, void* trace, fw_stream_t stream) {
+  int rc = check_decoder(d);
+  if (rc) return rc;
+  FW_REQUIRE(trace != nullptr, FW_ERR_NULL, "decoder_step_trace: trace is NULL");
+  FW_REQUIRE(aligned16(trace), FW_ERR_ALIGN, "decoder_step_trace: trace must be 16-byte aligned");
+  return decoder_one_step(d, static_cast<cudaStream_t>(stream), static_cast<half*>(trace));
 }
 
 }  // extern "C"

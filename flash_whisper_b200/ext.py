@@ -245,6 +245,19 @@ class Ext:
     def decoder_step(self, desc, steps=1):
         _lib.call('fw_decoder_step', ctypes.byref(desc), int(steps), _stream())
 
+    def decoder_launch(self, desc, layer, block):
+        """One launch of the decode step (block 0 self, 1 cross, 2 fc1, 3 fc2, 4 LM head)."""
+        _lib.call('fw_decoder_launch', ctypes.byref(desc), int(layer), int(block), _stream())
+
+    def decoder_step_trace(self, desc, trace):
+        """One decode step that also records each block's output into `trace` (fp16, at least
+        n_layers * TRACE_LAYER + 1280 elements; layout in include/flash_whisper.h)."""
+        _check_half(trace, 'trace')
+        need = desc.n_layers * _lib.TRACE_LAYER + HIDDEN
+        if trace.numel() < need:
+            raise RuntimeError(f'trace must hold at least {need} fp16 elements')
+        _lib.call('fw_decoder_step_trace', ctypes.byref(desc), _ptr(trace), _stream())
+
     def encoder_forward(self, desc):
         _lib.call('fw_encoder_forward', ctypes.byref(desc), _stream())
 

@@ -138,7 +138,9 @@ class CustomModel:
 
         self.dec_desc = self._decoder_desc()
         self.enc_desc = self._encoder_desc()
-        self.selftest = run_selftest(self.ext) if selftest else {'ok': None, 'checks': []}
+        self.selftest = run_selftest(self.ext, self) if selftest else {'ok': None, 'checks': []}
+        if selftest:
+            self.selftest['mel_max_abs_diff'] = self._mel_diff()
         self.graph_mel = self.graph_enc = self.graph_prompt = self.graph_chunk = None
         if capture:
             self._capture()
@@ -218,6 +220,21 @@ class CustomModel:
     def _chunk(self):
         self.ext.decoder_step(self.dec_desc, self.chunk)
 
+    def _mel_diff(self):
+        """Largest |GPU log-mel - transformers' WhisperFeatureExtractor| on 10 s of seeded noise, the
+        load-time front-end check of custom/model.py:77,100-105 (None if transformers is absent)."""
+        try:
+            from transformers import WhisperFeatureExtractor
+        except ImportError:
+            return None
+        audio = np.random.default_rng(0).standard_normal(10 * 16000).astype(np.float32) * 0.1
+        ref = WhisperFeatureExtractor(feature_size=self.dims.n_mels)(audio, sampling_rate=16000,
+                                                                      return_tensors='np').input_features[0]
+        self.load_audio(audio)
+        self._mel()
+        got = self.mel[1:-1].float().T.cpu().numpy()
+        return float(np.abs(got - ref).max())
+
     def _capture(self):
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -229,13 +246,32 @@ class CustomModel:
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         graphs = []
-        for fn in (self._mel, self._encode, self._prompt, self._chunk):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                fn()
+        for name, fn in (('mel', self._mel), ('encoder', self._encode), ('prompt', self._prompt),
+                         ('chunk', self._chunk)):
+            try:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn()
+            except Exception as exc:  # a stage whose capture fails runs eagerly (custom/model.py:165-168)
+                torch.cuda.synchronize()
+                g = None
+                self.selftest[f'{name}_graph'] = False
+                self.selftest[f'{name}_graph_error'] = f'{type(exc).__name__}: {exc}'
             graphs.append(g)
         torch.cuda.synchronize()
         self.graph_mel, self.graph_enc, self.graph_prompt, self.graph_chunk = graphs
+        if self.graph_enc is not None:
+            # graph replay vs eager on the same random input (custom/model.py:158-164)
+            mel_saved = self.mel.clone()
+            self.mel[1:-1].normal_()
+            self._encode()
+            eager = self.enc_out.clone()
+            self.enc_out.zero_()
+            self.graph_enc.replay()
+            torch.cuda.synchronize()
+            self.selftest['encoder_graph_max_abs_diff'] = float((self.enc_out.float() - eager.float()).abs().max())
+            self.selftest['encoder_graph'] = True
+            self.mel.copy_(mel_saved)
 
     def run_mel(self):
         self.graph_mel.replay() if self.graph_mel else self._mel()

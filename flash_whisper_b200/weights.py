@@ -150,6 +150,22 @@ def random_state_dict(seed=0, dims=TURBO, std=0.02, bias_std=0.0, ln_std=0.0, na
     return out
 
 
+def varied_state_dict(seed=0, dims=TURBO, decoder_std=0.05):
+    """Seeded weights whose greedy decode is not degenerate, for token-level parity tests.
+
+    With the HF init (std 0.02 everywhere, tied LM head) a random decoder's residual stream stays
+    dominated by the current token's embedding, so greedy decoding repeats one token and a token
+    match says little about the layers. Here the decoder weights are drawn with `decoder_std`, the
+    biases with std 0.02 and the LayerNorm parameters perturbed by 0.1, which makes the layers move the
+    argmax from step to step; the encoder keeps the HF init."""
+    names = param_shapes(dims)
+    enc = [n for n in names if not n.startswith('model.decoder')]
+    dec = [n for n in names if n.startswith('model.decoder')]
+    out = random_state_dict(seed, dims, names=enc)
+    out.update(random_state_dict(seed, dims, std=decoder_std, bias_std=0.02, ln_std=0.1, names=dec))
+    return out
+
+
 def load_hf_model(state_dict, dims=TURBO, dtype=torch.float32):
     """transformers WhisperForConditionalGeneration holding `state_dict` (oracle / CPU baseline)."""
     from transformers import WhisperForConditionalGeneration

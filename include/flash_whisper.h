@@ -79,7 +79,9 @@ int fw_decode_attention(const void* q, void* k, void* v, void* out, const int64_
  * heads * ceil(max_len / 64) <= 2048 head-splits and returns FW_ERR_SHAPE beyond that.
  * Semantics, arguments and results are otherwise those of fw_decode_attention. The first call on
  * each device looks up the array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture. All calls share the one array and nothing in it
+ * make that first call before any stream capture. The address is cached per device and context: the
+ * first call after a cudaDeviceReset (or in any new context of the device) looks it up again, so that
+ * call too must come before any stream capture. All calls share the one array and nothing in it
  * needs to start at zero (every split slot is written before the combine reads it), but calls
  * that overlap on the GPU (e.g. on two streams) race on it and must be serialised. */
 int fw_decode_attention_noalloc(const void* q, void* k, void* v, void* out, const int64_t* len_state,
@@ -187,6 +189,33 @@ typedef struct {
  * discarded; at state[0] == prompt_len - 1 first_mask applies and the prediction becomes tokens[0];
  * afterwards base_mask applies and each prediction is appended and fed back. */
 int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream);
+
+/* One launch of the decode step in isolation, as fw_decoder_step issues it (programmatic dependent
+ * launch included): block 0 = self-attention block of `layer`, 1 = cross-attention block, 2 = LN3 +
+ * fc1 + GELU, 3 = fc2 + residual, 4 = LM head (final LN, argmax, token bookkeeping; `layer` ignored).
+ * For per-kernel timing and profiling; a full step is blocks 0-3 of every layer, then block 4. No
+ * reference counterpart (the reference's step is custom/model.py:107-123 as one sequence). */
+int fw_decoder_launch(const fw_decoder_t* d, int layer, int block, fw_stream_t stream);
+
+/* Layout of the fw_decoder_step_trace buffer (fp16 element offsets): per layer l, at
+ * l * FW_TRACE_LAYER, the self-attention output, the residual stream after the self-attention block,
+ * the cross-attention output, the residual stream after the cross-attention block, the fc1 + GELU
+ * output and the residual stream after fc2; then, at n_layers * FW_TRACE_LAYER, the final LayerNorm
+ * row the LM head dotted. Total n_layers * FW_TRACE_LAYER + 1280 elements. */
+#define FW_TRACE_SELF_ATTN 0
+#define FW_TRACE_H_SELF 1280
+#define FW_TRACE_CROSS_ATTN 2560
+#define FW_TRACE_H_CROSS 3840
+#define FW_TRACE_FFN 5120
+#define FW_TRACE_H_FFN 10240
+#define FW_TRACE_LAYER 11520
+
+/* One decode step of fw_decoder_step (the same kernels, launch configurations and arithmetic) that
+ * also records every block's output into `trace` (fp16, 16-byte aligned, FW_TRACE_* layout), for
+ * activation-level parity checks of the fused step against a restatement of custom/model.py:107-123.
+ * The residual-stream snapshots are device-to-device copies enqueued between the launches, so the
+ * step is slower than fw_decoder_step; the results (cache writes, token, state) are identical. */
+int fw_decoder_step_trace(const fw_decoder_t* d, void* trace, fw_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * GPU log-mel front end (custom/model.py:93-98; WhisperFeatureExtractor semantics)

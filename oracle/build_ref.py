@@ -8,6 +8,9 @@ GPU tests load it with `load_ref()` to compare this package's kernels against th
 identical inputs. Nothing is copied from the reference into the repository.
 
     python -m oracle.build_ref [/path/to/reference]
+
+Without an argument the checkout is $FLASH_WHISPER_REFERENCE, else a directory named `reference` beside
+this repository's directory.
 """
 
 import importlib.machinery
@@ -21,7 +24,14 @@ REF_DIR = HERE / '_ref'
 SO_NAME = 'whisper_ext_ref'
 
 
-def build(reference=Path('/root/reference')):
+def reference_checkout():
+    """Path of the reference checkout ($FLASH_WHISPER_REFERENCE, else ../reference beside the repo)."""
+    env = os.environ.get('FLASH_WHISPER_REFERENCE')
+    return Path(env) if env else HERE.parent.parent / 'reference'
+
+
+def build(reference=None):
+    reference = reference_checkout() if reference is None else reference
     src = Path(reference) / 'custom' / 'kernels' / 'whisper_kernels.cu'
     if not src.exists():
         return None
@@ -52,5 +62,5 @@ def load_ref():
 
 
 if __name__ == '__main__':
-    out = build(Path(sys.argv[1]) if len(sys.argv) > 1 else Path('/root/reference'))
+    out = build(Path(sys.argv[1]) if len(sys.argv) > 1 else None)
     print(f'built {out}' if out else 'reference source not found; nothing built')

@@ -115,36 +115,66 @@ class WhisperOracle:
         self.cross_k, self.cross_v = np.stack(ks), np.stack(vs)
 
     # ---- decoder -------------------------------------------------------------------------
-    def step(self, token, pos):
-        """One decode step (custom/model.py:107-122): returns fp16-valued logits [vocab] (float32)."""
+    def embed(self, token, pos):
+        """Layer-0 input: fp16(embed_tokens[token] + embed_positions[pos]) (custom/model.py:110)."""
+        return self.r(self.w['model.decoder.embed_tokens.weight'][token] + self.w['model.decoder.embed_positions.weight'][pos])
+
+    def self_block(self, i, h, pos):
+        """LN1 -> q/k/v -> cache write at `pos` -> attention over pos + 1 keys -> out_proj -> residual
+        (custom/model.py:113-116). Returns (attention output, new h, k row, v row)."""
         d = self.dims
         hd, nh = d.head_dim, d.heads
-        scale = np.float32(hd ** -0.5)
-        h = self.r(self.w['model.decoder.embed_tokens.weight'][token] + self.w['model.decoder.embed_positions.weight'][pos])
-        for i in range(d.decoder_layers):
-            p = f'model.decoder.layers.{i}'
-            y = self.r(layer_norm(h, self.w[f'{p}.self_attn_layer_norm.weight'], self.w[f'{p}.self_attn_layer_norm.bias']))
-            q = self.r(linear(y, self.w[f'{p}.self_attn.q_proj.weight'], self.w[f'{p}.self_attn.q_proj.bias']))
-            k = self.r(linear(y, self.w[f'{p}.self_attn.k_proj.weight']))
-            v = self.r(linear(y, self.w[f'{p}.self_attn.v_proj.weight'], self.w[f'{p}.self_attn.v_proj.bias']))
-            self.self_k[i, :, pos] = k.reshape(nh, hd)
-            self.self_v[i, :, pos] = v.reshape(nh, hd)
-            K, V = self.self_k[i, :, :pos + 1], self.self_v[i, :, :pos + 1]
-            s = np.einsum('hd,hld->hl', q.reshape(nh, hd), K) * scale
-            attn = self.r(np.einsum('hl,hld->hd', softmax(s), V).reshape(-1))
-            h = self.r(h + self.r(linear(attn, self.w[f'{p}.self_attn.out_proj.weight'], self.w[f'{p}.self_attn.out_proj.bias'])))
-            y = self.r(layer_norm(h, self.w[f'{p}.encoder_attn_layer_norm.weight'],
-                               self.w[f'{p}.encoder_attn_layer_norm.bias']))
-            q = self.r(linear(y, self.w[f'{p}.encoder_attn.q_proj.weight'], self.w[f'{p}.encoder_attn.q_proj.bias']))
-            s = np.einsum('hd,hld->hl', q.reshape(nh, hd), self.cross_k[i]) * scale
-            attn = self.r(np.einsum('hl,hld->hd', softmax(s), self.cross_v[i]).reshape(-1))
-            h = self.r(h + self.r(linear(attn, self.w[f'{p}.encoder_attn.out_proj.weight'],
-                                   self.w[f'{p}.encoder_attn.out_proj.bias'])))
-            y = self.r(layer_norm(h, self.w[f'{p}.final_layer_norm.weight'], self.w[f'{p}.final_layer_norm.bias']))
-            f = self.r(gelu(self.r(linear(y, self.w[f'{p}.fc1.weight'], self.w[f'{p}.fc1.bias']))))
-            h = self.r(h + self.r(linear(f, self.w[f'{p}.fc2.weight'], self.w[f'{p}.fc2.bias'])))
+        p = f'model.decoder.layers.{i}'
+        y = self.r(layer_norm(h, self.w[f'{p}.self_attn_layer_norm.weight'], self.w[f'{p}.self_attn_layer_norm.bias']))
+        q = self.r(linear(y, self.w[f'{p}.self_attn.q_proj.weight'], self.w[f'{p}.self_attn.q_proj.bias']))
+        k = self.r(linear(y, self.w[f'{p}.self_attn.k_proj.weight']))
+        v = self.r(linear(y, self.w[f'{p}.self_attn.v_proj.weight'], self.w[f'{p}.self_attn.v_proj.bias']))
+        self.self_k[i, :, pos] = k.reshape(nh, hd)
+        self.self_v[i, :, pos] = v.reshape(nh, hd)
+        K, V = self.self_k[i, :, :pos + 1], self.self_v[i, :, :pos + 1]
+        s = np.einsum('hd,hld->hl', q.reshape(nh, hd), K) * np.float32(hd ** -0.5)
+        attn = self.r(np.einsum('hl,hld->hd', softmax(s), V).reshape(-1))
+        h = self.r(h + self.r(linear(attn, self.w[f'{p}.self_attn.out_proj.weight'], self.w[f'{p}.self_attn.out_proj.bias'])))
+        return attn, h, k, v
+
+    def cross_block(self, i, h):
+        """LN2 -> cross q -> attention over the encoder cache -> out_proj -> residual
+        (custom/model.py:116-119). Returns (attention output, new h)."""
+        d = self.dims
+        hd, nh = d.head_dim, d.heads
+        p = f'model.decoder.layers.{i}'
+        y = self.r(layer_norm(h, self.w[f'{p}.encoder_attn_layer_norm.weight'], self.w[f'{p}.encoder_attn_layer_norm.bias']))
+        q = self.r(linear(y, self.w[f'{p}.encoder_attn.q_proj.weight'], self.w[f'{p}.encoder_attn.q_proj.bias']))
+        s = np.einsum('hd,hld->hl', q.reshape(nh, hd), self.cross_k[i]) * np.float32(hd ** -0.5)
+        attn = self.r(np.einsum('hl,hld->hd', softmax(s), self.cross_v[i]).reshape(-1))
+        h = self.r(h + self.r(linear(attn, self.w[f'{p}.encoder_attn.out_proj.weight'],
+                                     self.w[f'{p}.encoder_attn.out_proj.bias'])))
+        return attn, h
+
+    def fc1(self, i, h):
+        """LN3 -> fc1 -> GELU (custom/model.py:119-120)."""
+        p = f'model.decoder.layers.{i}'
+        y = self.r(layer_norm(h, self.w[f'{p}.final_layer_norm.weight'], self.w[f'{p}.final_layer_norm.bias']))
+        return self.r(gelu(self.r(linear(y, self.w[f'{p}.fc1.weight'], self.w[f'{p}.fc1.bias']))))
+
+    def fc2(self, i, h, f):
+        """fc2 -> residual (custom/model.py:120-121)."""
+        p = f'model.decoder.layers.{i}'
+        return self.r(h + self.r(linear(f, self.w[f'{p}.fc2.weight'], self.w[f'{p}.fc2.bias'])))
+
+    def final(self, h):
+        """Final LayerNorm and fp16 logits over the tied vocab matrix (custom/model.py:122)."""
         y = self.r(layer_norm(h, self.w['model.decoder.layer_norm.weight'], self.w['model.decoder.layer_norm.bias']))
-        return self.r(self.w['model.decoder.embed_tokens.weight'] @ y)
+        return y, self.r(self.w['model.decoder.embed_tokens.weight'] @ y)
+
+    def step(self, token, pos):
+        """One decode step (custom/model.py:107-122): returns fp16-valued logits [vocab] (float32)."""
+        h = self.embed(token, pos)
+        for i in range(self.dims.decoder_layers):
+            _, h, _, _ = self.self_block(i, h, pos)
+            _, h = self.cross_block(i, h)
+            h = self.fc2(i, h, self.fc1(i, h))
+        return self.final(h)[1]
 
     def greedy(self, n_tokens, prompt, base_mask=None, first_mask=None, forced=None):
         """Greedy decode after the prompt (custom/model.py:196-215, EOS ignored).

@@ -14,7 +14,16 @@ Fixtures (all small):
                       of the reference's PyTorch loop (custom/pytorch_model.py:59-80 semantics, CPU fp32)
   turbo_tokens.json   the same loop at full large-v3-turbo size, seed-0 weights and seed-0 30 s audio,
                       forced to 32 tokens
+  turbo_tokens_varied.json
+                      the same loop on flash_whisper_b200.weights.varied_state_dict(0) (a decoder whose
+                      greedy output changes from step to step), seed-1 30 s audio, 32 tokens, with the
+                      fp32 top-2 logit gap of every step. The two token fixtures need only
+                      transformers: `python tests/golden/make_golden.py --tokens-only`
+
+The reference checkout is the first argument, or $FLASH_WHISPER_REFERENCE.
 """
+
+import os
 
 import json
 import sys
@@ -94,16 +103,56 @@ def main(reference):
     np.savez_compressed(HERE / 'hf_small.npz', enc_rows=enc[::100].numpy(), enc_sum=enc.double().sum().numpy(),
                         prompt_logits=logits.numpy(), tokens=np.array(tokens), seed=3, audio_seed=1)
 
-    sd = random_state_dict(0, TURBO)
-    model = load_hf_model(sd, TURBO)
+    make_turbo_tokens()
+    make_varied_tokens()
+
+
+def make_turbo_tokens():
+    """32 greedy tokens of the CPU fp32 reference loop at full size with the HF-init weights (seed 0)."""
+    from flash_whisper_b200.audio import synthetic_audio
+    from flash_whisper_b200.weights import TURBO, load_hf_model, random_state_dict
+    from oracle.hf_cpu import transcribe_cpu
+
+    model = load_hf_model(random_state_dict(0, TURBO), TURBO)
     audio = synthetic_audio(0, 30.0)
-    tokens, timing = transcribe_cpu(model, audio, TURBO, n_tokens=32, begin_suppress=TURBO.begin_suppress)
+    gaps = []
+    tokens, timing = transcribe_cpu(model, audio, TURBO, n_tokens=32, begin_suppress=TURBO.begin_suppress,
+                                    logit_gaps=gaps)
     (HERE / 'turbo_tokens.json').write_text(json.dumps({
         'weights_seed': 0, 'audio_seed': 0, 'seconds': 30.0, 'n_tokens': 32, 'tokens': tokens,
-        'generator': 'oracle.hf_cpu.transcribe_cpu (custom/pytorch_model.py loop, CPU fp32)',
+        'top2_gap': [round(g, 6) for g in gaps],
+        'generator': 'oracle.hf_cpu.transcribe_cpu (custom/pytorch_model.py loop, CPU fp32, HF feature extractor)',
         'timing_s': {k: round(v, 4) for k, v in timing.items() if k.endswith('_s')}}, indent=1) + '\n')
-    print('tokens', tokens, timing)
+    print('tokens', tokens, 'min gap', min(gaps))
+
+
+def make_varied_tokens():
+    """32 greedy tokens of the CPU fp32 reference loop on weights whose output is not degenerate."""
+    from flash_whisper_b200.audio import synthetic_audio
+    from flash_whisper_b200.weights import TURBO, load_hf_model, varied_state_dict
+    from oracle.hf_cpu import transcribe_cpu
+
+    model = load_hf_model(varied_state_dict(0, TURBO), TURBO)
+    audio = synthetic_audio(1, 30.0)
+    gaps = []
+    tokens, timing = transcribe_cpu(model, audio, TURBO, n_tokens=32, begin_suppress=TURBO.begin_suppress,
+                                    logit_gaps=gaps)
+    (HERE / 'turbo_tokens_varied.json').write_text(json.dumps({
+        'weights': 'varied_state_dict(0)', 'audio_seed': 1, 'seconds': 30.0, 'n_tokens': 32, 'tokens': tokens,
+        'top2_gap': [round(g, 6) for g in gaps],
+        'generator': 'oracle.hf_cpu.transcribe_cpu (custom/pytorch_model.py loop, CPU fp32, HF feature extractor)',
+        'timing_s': {k: round(v, 4) for k, v in timing.items() if k.endswith('_s')}}, indent=1) + '\n')
+    print('varied tokens', tokens, 'min gap', min(gaps))
 
 
 if __name__ == '__main__':
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path('/root/reference'))
+    if '--varied-only' in sys.argv:
+        make_varied_tokens()
+    elif '--tokens-only' in sys.argv:
+        make_turbo_tokens()
+        make_varied_tokens()
+    else:
+        ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('FLASH_WHISPER_REFERENCE')
+        if not ref:
+            sys.exit('usage: make_golden.py /path/to/reference  (or set FLASH_WHISPER_REFERENCE)')
+        main(Path(ref))

@@ -1,0 +1,162 @@
+"""Activation-level parity of the fused decode step (the kernels fw_decoder_step runs in production)
+against the numpy restatement of custom/model.py:107-123 (oracle/model_np.py).
+
+fw_decoder_step_trace runs one step with the production kernels and launch configuration and records
+every block's output. Each block is checked against the oracle fed the GPU's own input of that
+block, so a mismatch names the kernel:
+
+  * head_block_kernel<self> (LN1, q/k/v, cache write, split attention, out_proj, residual): the
+    attention output and the new residual stream; the K/V row it writes into the cache must equal,
+    bit for bit, what the stand-alone fw_ln_gemv computes for the same h (same LayerNorm and dot
+    arithmetic), and match the oracle's within tolerance;
+  * head_block_kernel<cross>: attention output and residual stream;
+  * ln_gemv_kernel (LN3 + fc1 + GELU) and gemv_residual_kernel (fc2 + residual);
+  * the LayerNorm fused into lm_head_q_kernel, the chosen token (bit-exact against the full fp16 LM
+    head on the same row) and the token bookkeeping.
+
+The self-attention length L = position + 1 is reached by seeding the self cache below the position
+and the state, at L in {1, 64, 224, 448} (BASELINE config 1's lengths; 448 is the last position).
+Tolerance: rtol 1e-2, atol 1e-3 on fp16 activations; bit-exact for the cache
+rows and the argmax. Weights come from varied_state_dict, whose decoder moves the argmax from step
+to step, with random biases and LayerNorm parameters so every bias and LN path carries signal.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from flash_whisper_b200 import _lib
+from flash_whisper_b200.weights import TURBO, varied_state_dict
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-2, 1e-3
+
+
+@pytest.fixture(scope='module')
+def varied_sd():
+    return varied_state_dict(0, TURBO)
+
+
+@pytest.fixture(scope='module')
+def traced_model(cuda, varied_sd):
+    from flash_whisper_b200.model import CustomModel
+    model = CustomModel(state_dict=varied_sd, dims=TURBO, selftest=False, capture=False)
+    g = torch.Generator(device='cuda').manual_seed(7)
+    model.cross_kv.copy_((torch.randn(model.cross_kv.shape, generator=g, device='cuda') * 0.5).half())
+    return model
+
+
+@pytest.fixture(scope='module')
+def oracle_w(varied_sd):
+    from oracle.model_np import WhisperOracle
+    return WhisperOracle(varied_sd, TURBO, decoder_only=True)
+
+
+def _close(name, got, want, rtol=RTOL, atol=ATOL):
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    err = np.abs(got - want)
+    bad = err > atol + rtol * np.abs(want)
+    assert not bad.any(), (f'{name}: {int(bad.sum())} of {bad.size} outside rtol {rtol} / atol {atol}, '
+                           f'max abs err {float(err.max()):.3e}')
+
+
+def _np(t):
+    return t.float().cpu().numpy()
+
+
+@pytest.mark.parametrize('length', [1, 64, 224, 448])
+def test_fused_decode_step_activations_vs_oracle(traced_model, oracle_w, length):
+    from oracle.model_np import linear, r16
+    model, o, d = traced_model, oracle_w, TURBO
+    pos = length - 1
+    g = torch.Generator(device='cuda').manual_seed(100 + length)
+    model.self_kv.copy_((torch.randn(model.self_kv.shape, generator=g, device='cuda') * 0.5).half())
+    cur = int(torch.randint(0, d.vocab, (1,), generator=g, device='cuda'))
+    count = 5
+    model.state.copy_(torch.tensor([pos, count]))
+    model.cur.fill_(cur)
+    model.tokens.zero_()
+    model.best.zero_()
+    o.self_k = _np(model.self_kv[:, 0]).copy()
+    o.self_v = _np(model.self_kv[:, 1]).copy()
+    o.cross_k = _np(model.cross_kv[:, 0])
+    o.cross_v = _np(model.cross_kv[:, 1])
+    cache_before = model.self_kv.clone()
+    token_in = d.prompt[pos] if pos < len(d.prompt) else cur
+
+    trace = torch.zeros(d.decoder_layers * _lib.TRACE_LAYER + d.d_model, dtype=torch.float16, device='cuda')
+    model.ext.decoder_step_trace(model.dec_desc, trace)
+    torch.cuda.synchronize()
+    assert model.ext.device_error() == 0
+    tr = _np(trace)
+
+    # Stage by stage, the oracle gets the GPU's input of each block.
+    h_in = o.embed(token_in, pos)
+    chain = h_in.copy()  # the oracle's own chain, for the end-to-end comparison below
+    for i in range(d.decoder_layers):
+        t = tr[i * _lib.TRACE_LAYER:(i + 1) * _lib.TRACE_LAYER]
+        p = f'model.decoder.layers.{i}'
+        # self-attention block
+        attn_ref, _, k_ref, v_ref = o.self_block(i, h_in, pos)
+        attn_gpu = t[_lib.TRACE_SELF_ATTN:_lib.TRACE_SELF_ATTN + 1280]
+        _close(f'layer {i} self attention', attn_gpu, attn_ref)
+        h_self_ref = r16(h_in + r16(linear(attn_gpu, o.w[f'{p}.self_attn.out_proj.weight'],
+                                           o.w[f'{p}.self_attn.out_proj.bias'])))
+        h_self = t[_lib.TRACE_H_SELF:_lib.TRACE_H_SELF + 1280]
+        _close(f'layer {i} h after self block', h_self, h_self_ref)
+        # the fused cache write: bit-identical to the stand-alone LN + q/k/v GEMV on the same h
+        L = model.dec.layers[i]
+        qkv = torch.empty(3 * d.d_model, dtype=torch.float16, device='cuda')
+        model.ext.ln_gemv(torch.from_numpy(h_in).half().cuda(), L.ln1[0], L.ln1[1], d.eps, L.qkv_w, L.qkv_b, qkv)
+        k_row = model.self_kv[i, 0, :, pos].reshape(-1)
+        v_row = model.self_kv[i, 1, :, pos].reshape(-1)
+        assert torch.equal(k_row, qkv[1280:2560]) and torch.equal(v_row, qkv[2560:]), f'layer {i} cache write'
+        _close(f'layer {i} written K row', _np(k_row), k_ref)
+        _close(f'layer {i} written V row', _np(v_row), v_ref)
+        untouched = torch.ones(d.max_pos, dtype=torch.bool, device='cuda')
+        untouched[pos] = False
+        assert torch.equal(model.self_kv[i, :, :, untouched], cache_before[i, :, :, untouched]), f'layer {i} rows'
+        # cross-attention block
+        cattn_ref, _ = o.cross_block(i, h_self)
+        cattn_gpu = t[_lib.TRACE_CROSS_ATTN:_lib.TRACE_CROSS_ATTN + 1280]
+        _close(f'layer {i} cross attention', cattn_gpu, cattn_ref)
+        h_cross_ref = r16(h_self + r16(linear(cattn_gpu, o.w[f'{p}.encoder_attn.out_proj.weight'],
+                                              o.w[f'{p}.encoder_attn.out_proj.bias'])))
+        h_cross = t[_lib.TRACE_H_CROSS:_lib.TRACE_H_CROSS + 1280]
+        _close(f'layer {i} h after cross block', h_cross, h_cross_ref)
+        # fc1 + GELU, fc2 + residual
+        ffn = t[_lib.TRACE_FFN:_lib.TRACE_FFN + 5120]
+        _close(f'layer {i} fc1+gelu', ffn, o.fc1(i, h_cross))
+        h_out = t[_lib.TRACE_H_FFN:_lib.TRACE_H_FFN + 1280]
+        _close(f'layer {i} h after fc2', h_out, o.fc2(i, h_cross, ffn))
+        h_in = h_out
+        # oracle chain (its own inputs throughout)
+        _, chain, _, _ = o.self_block(i, chain, pos)
+        _, chain = o.cross_block(i, chain)
+        chain = o.fc2(i, chain, o.fc1(i, chain))
+    _close("final residual stream vs the oracle chain", h_in, chain)
+
+    y_gpu = tr[d.decoder_layers * _lib.TRACE_LAYER:]
+    y_ref, logits = o.final(h_in)
+    _close('final LayerNorm', y_gpu, y_ref)
+
+    # token: bit-exact against the full fp16 LM head on the GPU's own row, and the oracle's argmax up
+    # to an fp16 near-tie (two fp16 ulps of a logit near 4)
+    best = torch.zeros(1, dtype=torch.long, device='cuda')
+    mask = model.first_mask if pos == len(d.prompt) - 1 else model.base_mask
+    model.ext.lm_head_argmax(torch.from_numpy(y_gpu).half().cuda(), model.dec.lm_head, mask, best)
+    want_tok = 0xFFFFFFFF - (int(best) & 0xFFFFFFFF)
+    assert int(model.cur) == want_tok
+    masked = logits.copy()
+    masked[_np(mask).astype(bool)] = -np.inf
+    assert masked.max() - masked[want_tok] <= 4e-3
+    # bookkeeping (custom/model.py:197-207 prompt handling, whisper_kernels.cu:90-100 finalize)
+    state = model.state.tolist()
+    assert state[0] == min(pos + 1, d.max_pos - 1)
+    if pos < len(d.prompt) - 1:
+        assert state[1] == count and int(model.tokens.abs().sum()) == 0
+    else:
+        assert state[1] == count + 1 and int(model.tokens[count]) == want_tok
+    assert int(model.best) == 0

@@ -28,7 +28,14 @@ def model(cuda, turbo_sd):
 
 
 def test_model_selftest_and_graphs(model):
-    assert model.selftest['ok'], model.selftest
+    """Load-time checks (custom/model.py:76-77,149-171): kernel self-test incl. one traced step of the
+    model's own fused decoder, GPU log-mel vs transformers' feature extractor, and the captured encoder
+    graph replaying the eager encoder bit for bit."""
+    st = model.selftest
+    assert st['ok'], [c for c in st['checks'] if not c['ok']]
+    assert any(c['name'].startswith('decoder ') for c in st['checks'])
+    assert st['mel_max_abs_diff'] is not None and st['mel_max_abs_diff'] < 2e-2, st['mel_max_abs_diff']
+    assert st['encoder_graph'] is True and st['encoder_graph_max_abs_diff'] == 0.0
     assert model.graph_chunk is not None and model.graph_enc is not None
 
 
@@ -46,18 +53,40 @@ def test_transcribe_surface_and_validation(model):
     assert out['n_tokens'] == len(out['token_ids']) <= 20
 
 
-def test_forced_tokens_vs_cpu_reference_golden(model):
-    gold = json.loads((GOLDEN / 'turbo_tokens.json').read_text())
-    out = model.transcribe(synthetic_audio(gold['audio_seed'], gold['seconds']), max_new_tokens=32,
+def _golden_match(model, fixture):
+    gold = json.loads((GOLDEN / fixture).read_text())
+    out = model.transcribe(synthetic_audio(gold['audio_seed'], gold['seconds']), max_new_tokens=gold['n_tokens'],
                            stop_at_eos=False)
-    match = sum(a == b for a, b in zip(out['token_ids'], gold['tokens']))
-    print('fp16 GPU vs fp32 CPU reference tokens match', match, '/ 32')
-    assert out['token_ids'][0] == gold['tokens'][0]
-    assert match >= 30
+    got, want = out['token_ids'], gold['tokens']
+    first_diff = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
+    print(f'{fixture}: fp16 GPU vs fp32 CPU reference, first divergence at {first_diff}, '
+          f'fp32 top-2 gaps {gold["top2_gap"][:8]}')
+    return got, want, first_diff
+
+
+def test_forced_tokens_vs_cpu_reference_golden(model):
+    """The CPU fp32 reference loop (custom/pytorch_model.py on transformers) and this fp16 pipeline
+    agree token for token on HF-init weights (fp32 top-2 gaps >= 0.13 at every step)."""
+    got, want, first_diff = _golden_match(model, 'turbo_tokens.json')
+    assert first_diff is None
+
+
+def test_varied_tokens_vs_cpu_reference_golden(cuda):
+    """Same, on weights whose greedy output is not one repeated token (varied_state_dict)."""
+    from flash_whisper_b200.model import CustomModel
+    from flash_whisper_b200.weights import varied_state_dict
+    m = CustomModel(state_dict=varied_state_dict(0, TURBO), dims=TURBO, selftest=False)
+    got, want, first_diff = _golden_match(m, 'turbo_tokens_varied.json')
+    assert len(set(want)) > 8  # the fixture is not degenerate
+    assert first_diff is None
+    del m
+    torch.cuda.empty_cache()
 
 
 def test_decode_step_vs_numpy_oracle(model, turbo_sd):
-    """Teacher-forced: every GPU token must be the oracle's argmax up to fp16 near-ties."""
+    """Teacher-forced: every GPU token must be the oracle's argmax, except at a step whose oracle
+    top-2 gap is itself an fp16 near-tie (<= 4e-3, two fp16 ulps of a logit near 4), where the
+    chosen token must be within that gap of the maximum."""
     from oracle.model_np import WhisperOracle
     n = 24
     out = model.transcribe(synthetic_audio(2, 30.0), max_new_tokens=n, stop_at_eos=False)
@@ -67,8 +96,8 @@ def test_decode_step_vs_numpy_oracle(model, turbo_sd):
     first = np.isin(np.arange(TURBO.vocab), TURBO.begin_suppress)
     tokens, gaps, chosen_gap = o.greedy(n, list(TURBO.prompt), None, first, forced=out['token_ids'])
     assert max(chosen_gap) <= 4e-3, (chosen_gap, gaps)
-    exact = sum(a == b for a, b in zip(tokens, out['token_ids']))
-    assert exact >= n - 1
+    for i, (a, b) in enumerate(zip(tokens, out['token_ids'])):
+        assert a == b or gaps[i] <= 4e-3, f'step {i}: oracle {a} (gap {gaps[i]:.3e}), GPU {b}'
 
 
 def test_tokens_bitexact_vs_reference_cuda_backend(model, turbo_sd):
@@ -84,6 +113,31 @@ def test_tokens_bitexact_vs_reference_cuda_backend(model, turbo_sd):
         first_diff = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
         assert got == want, f'seed {seed}: first divergence at step {first_diff}'
     del ref
+    torch.cuda.empty_cache()
+
+
+def test_varied_tokens_bitexact_vs_reference_cuda_backend(cuda):
+    """224 greedy tokens on weights whose output changes every few steps, identical to the
+    reference's CUDA backend (its own kernels + cuBLAS projections) on the same weights and audio."""
+    from oracle.build_ref import load_ref
+    if load_ref() is None:
+        pytest.skip('oracle/_ref not built')
+    from flash_whisper_b200.model import CustomModel
+    from flash_whisper_b200.weights import varied_state_dict
+    from oracle.ref_pipeline import RefCudaBackend
+    sd = varied_state_dict(0, TURBO)
+    ref = RefCudaBackend(sd, TURBO)
+    audio = synthetic_audio(3, 30.0)
+    want, _ = ref.transcribe(audio, 224)
+    del ref
+    torch.cuda.empty_cache()
+    m = CustomModel(state_dict=sd, dims=TURBO, selftest=False)
+    got = m.transcribe(audio, max_new_tokens=224, stop_at_eos=False)['token_ids']
+    first_diff = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
+    print('varied weights: distinct tokens', len(set(want)), 'first divergence', first_diff)
+    assert len(set(want)) > 20
+    assert got == want, f'first divergence at step {first_diff}'
+    del m
     torch.cuda.empty_cache()
 
 
