@@ -46,6 +46,24 @@ class Decoder(ctypes.Structure):
     ]
 
 
+MAX_CLIPS = 8
+
+
+class BatchDecoder(ctypes.Structure):
+    _fields_ = [
+        ('n_layers', c_int), ('heads', c_int), ('max_pos', c_int), ('enc_len', c_int), ('vocab', c_int),
+        ('prompt_len', c_int), ('clips', c_int), ('eps', c_float), ('scale', c_float),
+        ('embed', vp), ('pos_embed', vp), ('lm_head', vp), ('final_g', vp), ('final_b', vp),
+        ('base_mask', vp), ('first_mask', vp), ('prompt', vp),
+        ('layers', DecoderLayer * MAX_LAYERS),
+        ('self_clip_stride', c_int64), ('cross_clip_stride', c_int64),
+        ('h', vp), ('qkv', vp), ('attn', vp), ('ffn', vp),
+        ('part_m', vp), ('part_l', vp), ('part_acc', vp), ('ws_splits', c_int64),
+        ('counters', vp), ('cur', vp), ('state', vp), ('tokens', vp), ('best', vp), ('n_tokens', c_int64),
+        ('lm_q', vp), ('lm_rp', vp),
+    ]
+
+
 class EncoderLayer(ctypes.Structure):
     _fields_ = [(name, vp) for name in (
         'ln1_g', 'ln1_b', 'ln2_g', 'ln2_b', 'qkv_w', 'qkv_b', 'out_w', 'out_b', 'fc1_w', 'fc1_b', 'fc2_w', 'fc2_b')]
@@ -84,6 +102,7 @@ _SIGNATURES = {
     'fw_decoder_step': (c_int, [POINTER(Decoder), c_int, vp]),
     'fw_decoder_step_trace': (c_int, [POINTER(Decoder), vp, vp]),
     'fw_decoder_launch': (c_int, [POINTER(Decoder), c_int, c_int, vp]),
+    'fw_batch_decoder_step': (c_int, [POINTER(BatchDecoder), c_int, vp]),
     'fw_log_mel': (c_int, [vp, c_int, c_int, vp, vp, vp, vp, c_int, vp]),
     'fw_gemm_f16': (c_int, [vp, c_int64, vp, c_int64, vp, vp, c_int64, vp, c_int64, c_int, c_int, c_int, c_int,
                             c_float, c_int, vp]),

@@ -199,6 +199,9 @@ struct AttnParams {
   float* part_acc;
   half* out;
   unsigned int* counters;
+  // Batched decode: clip z = blockIdx.z reads and writes at these element offsets times z (zero
+  // for a single clip); its split partials and arrival counters follow clip z-1's.
+  int64_t clip_q, clip_kv, clip_new, clip_out, clip_state;
 };
 
 constexpr int kMaxSplits = 128;  // max_len <= 8192 keys
@@ -405,6 +408,22 @@ __global__ void __launch_bounds__(64) attn_split_kernel(AttnParams p) {
   const int head = blockIdx.x;
   const int split = blockIdx.y;
   const int splits = gridDim.y;
+  const int z = blockIdx.z;
+  if (z > 0) {
+    p.q += z * p.clip_q;
+    p.k += z * p.clip_kv;
+    p.v += z * p.clip_kv;
+    if (p.k_new) {
+      p.k_new += z * p.clip_new;
+      p.v_new += z * p.clip_new;
+    }
+    if (p.len_state) p.len_state += z * p.clip_state;
+    p.out += z * p.clip_out;
+    p.part_m += static_cast<size_t>(z) * gridDim.x * splits;
+    p.part_l += static_cast<size_t>(z) * gridDim.x * splits;
+    p.part_acc += static_cast<size_t>(z) * gridDim.x * splits * kHeadDim;
+    if (p.counters) p.counters += z * gridDim.x;
+  }
   const int slot = head * splits + split;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
 
@@ -870,6 +889,9 @@ struct LmParams {
   int max_pos;
   int prompt_len;
   half* y_out;  // optional [1280]: CTA 0 writes the (LayerNorm) input row it dotted (fw_decoder_step_trace)
+  // batched decode (lm_head_q_kernel<.., .., kClips > 1>): clip count and row stride of tokens
+  int clips;
+  int64_t tokens_stride;
 };
 
 // Token bookkeeping shared by argmax_finalize and the fused LM-head tail.
@@ -1041,8 +1063,6 @@ constexpr int kQBoxRows = 32;                           // rows per TMA box
 constexpr int kQChunk = 128;                            // K bytes per stage (one 128-byte swizzle row)
 constexpr int kQChunks = kHidden / kQChunk;             // 10 stages per tile
 constexpr int kQStageBytes = kQTileRows * kQChunk;      // 16 KB
-constexpr int kQXBytes = kQChunks * 8 * kQChunk;        // B operand: 8 rows (x_hi, x_lo, 0...) x 1280
-constexpr int kQSmem = kQStages * kQStageBytes + kQXBytes + 1024;
 constexpr float kXqMax = 8191.f;
 
 __device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -1107,14 +1127,32 @@ __device__ __forceinline__ void dot1280_ptrs(const half* const (&rows)[kRows], c
   for (int r = 0; r < kRows; ++r) out[r] = acc[r];
 }
 
+// Shape of lm_head_q_kernel for up to kClips clips: the B operand holds (x_hi, x_lo) of every clip
+// in rows 2c, 2c + 1 (MMA N = 8 for one clip, 16 for up to eight), the accumulator of each tile is
+// N TMEM columns (two buffers), and the per-clip arrays live in dynamic shared memory after the
+// stage ring.
+template <int kClips>
+struct LmqShape {
+  static constexpr int kN = 2 * kClips <= 8 ? 8 : 16;
+  static constexpr int kXBytes = kQChunks * kN * kQChunk;
+  static constexpr int kYsOff = kQStages * kQStageBytes + kXBytes;
+  static constexpr int kUbOff = kYsOff + kClips * kHidden * 2;
+  static constexpr int kCandOff = kUbOff + kClips * kLmMaxRowsPerCta * 4;
+  static constexpr int kSmem = kCandOff + kClips * kLmMaxRowsPerCta * 2 + 1024;
+  static constexpr uint32_t kTmemCols = 2 * kN <= 32 ? 32 : 64;
+};
+
 // Warp roles: warp 0 streams the CTA's int8 rows (32-row x 128-byte TMA boxes, 128B swizzle) through
 // a kQStages ring, the first stages requested before the PDL wait; warp 1 owns TMEM and issues
-// tcgen05.mma kind::i8 (M = 128 rows, N = 8, K = 32) of each tile against the B operand
-// [x_hi; x_lo; 0 ...] (xq = 128 x_hi + x_lo, both int8) into one of two TMEM accumulators; warps 2-5
-// read each row's two int32 sums (tcgen05.ld, TMEM lane = row) and form approx_r and B_r; all
-// eight warps then select and rescore the surviving rows.
-template <bool kLN, bool kFinalize>
+// tcgen05.mma kind::i8 (M = 128 rows, N = 8 or 16, K = 32) of each tile against the B operand
+// [x_hi; x_lo] of every clip (xq = 128 x_hi + x_lo, both int8) into one of two TMEM accumulators;
+// warps 2-5 read each row's two int32 sums per clip (tcgen05.ld, TMEM lane = row) and form approx_r
+// and B_r; all eight warps then select and rescore the surviving rows of each clip. kClips > 1 is the
+// batched decode step (p.clips <= kClips clips; clip c's LayerNorm input at p.h + 1280 c, its key at
+// p.best[c], its bookkeeping at p.state + 2c, p.cur + c and p.tokens + c * p.tokens_stride).
+template <bool kLN, bool kFinalize, int kClips>
 __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant__ CUtensorMap tmW, LmParams p) {
+  using S = LmqShape<kClips>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[kQStages];
   __shared__ __align__(8) uint64_t empty[kQStages];
@@ -1122,20 +1160,21 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ float red[16];
-  __shared__ __align__(16) half ys[kHidden];
   __shared__ __align__(16) float4 rps[kLmMaxRowsPerCta];
-  __shared__ float ub[kLmMaxRowsPerCta];
-  __shared__ unsigned short cand[kLmMaxRowsPerCta];
   __shared__ uint8_t msk[2][kLmMaxRowsPerCta];
-  __shared__ float warp_l[8], warp_b[8], xstat[2][8];
-  __shared__ unsigned long long warp_best[8];
-  __shared__ int ncand;
-  __shared__ unsigned s_lo_max;  // running max of the lower bounds (order-preserving bits)
+  __shared__ float warp_l[kClips][8], warp_b[kClips][8], xstat[kClips][2][8];
+  __shared__ unsigned long long warp_best[kClips][8];
+  __shared__ int ncand[kClips];
+  __shared__ unsigned s_lo_max[kClips];  // running max of the lower bounds (order-preserving bits)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* stages = smem_raw + (base - raw);
   uint8_t* xb = stages + kQStages * kQStageBytes;
+  half* ys = reinterpret_cast<half*>(stages + S::kYsOff);                // [kClips][1280]
+  float* ub = reinterpret_cast<float*>(stages + S::kUbOff);              // [kClips][kLmMaxRowsPerCta]
+  unsigned short* cand = reinterpret_cast<unsigned short*>(stages + S::kCandOff);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int C = kClips == 1 ? 1 : p.clips;
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int r1 = min(p.vocab, r0 + p.rows_per_cta);
   const int nrows = max(0, r1 - r0);
@@ -1165,7 +1204,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
     for (int it = 0; it < kQStages && it < total; ++it) issue(it, policy);  // weights: before the wait
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_sh, 32);
+    tmem_alloc(&tmem_base_sh, S::kTmemCols);
     tmem_relinquish();
   }
   // Constant per-row data (suppress flags, scales and bounds) and the zero rows of B.
@@ -1174,10 +1213,10 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
     msk[1][i] = p.first_mask ? static_cast<uint8_t>(p.first_mask[r0 + i]) : 0;
     rps[i] = p.rp[r0 + i];
   }
-  for (int i = threadIdx.x; i < kQXBytes / 16; i += 256) reinterpret_cast<uint4*>(xb)[i] = make_uint4(0, 0, 0, 0);
-  if (threadIdx.x == 0) {
-    ncand = 0;
-    s_lo_max = float_to_ordered(-INFINITY);
+  for (int i = threadIdx.x; i < S::kXBytes / 16; i += 256) reinterpret_cast<uint4*>(xb)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x < kClips) {
+    ncand[threadIdx.x] = 0;
+    s_lo_max[threadIdx.x] = float_to_ordered(-INFINITY);
   }
   float g[5], be[5];
   if (kLN) {
@@ -1194,37 +1233,42 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   pdl_wait();
   pdl_trigger();
 
-  float xv[5];
-  if (kLN) {
+  // LayerNorm of each clip's row (ln1280_stats order; consecutive calls may share `red`), its
+  // max|x| and |x|_1, and the B operand rows 2c (x_hi) and 2c + 1 (x_lo) of xq = rint(x / sx).
+  float xv[kClips][5];
 #pragma unroll
-    for (int i = 0; i < 5; ++i) xv[i] = __half2float(p.h[threadIdx.x + i * 256]);
-    float mean, inv;
-    ln1280_stats(xv, red, p.eps, mean, inv);
+  for (int c = 0; c < kClips; ++c) {
+    if (c >= C) break;
+    const half* hc = p.h + c * kHidden;
+    half* yc = ys + c * kHidden;
+    if (kLN) {
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const half y = __float2half(ln_apply(xv[i], mean, inv, g[i], be[i]));
-      ys[threadIdx.x + i * 256] = y;
-      xv[i] = __half2float(y);
+      for (int i = 0; i < 5; ++i) xv[c][i] = __half2float(hc[threadIdx.x + i * 256]);
+      float mean, inv;
+      ln1280_stats(xv[c], red, p.eps, mean, inv);
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        const half y = __float2half(ln_apply(xv[c][i], mean, inv, g[i], be[i]));
+        yc[threadIdx.x + i * 256] = y;
+        xv[c][i] = __half2float(y);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        const half y = hc[threadIdx.x + i * 256];
+        yc[threadIdx.x + i * 256] = y;
+        xv[c][i] = __half2float(y);
+      }
     }
-  } else {
+    if (kClips == 1 && p.y_out && blockIdx.x == 0) {
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const half y = p.h[threadIdx.x + i * 256];
-      ys[threadIdx.x + i * 256] = y;
-      xv[i] = __half2float(y);
+      for (int i = 0; i < 5; ++i) p.y_out[threadIdx.x + i * 256] = __float2half(xv[c][i]);
     }
-  }
-  if (p.y_out && blockIdx.x == 0) {
-#pragma unroll
-    for (int i = 0; i < 5; ++i) p.y_out[threadIdx.x + i * 256] = __float2half(xv[i]);
-  }
-  // max|x| and |x|_1 of the fp16 LayerNorm output
-  {
     float mx = 0.f, sm = 0.f;
 #pragma unroll
     for (int i = 0; i < 5; ++i) {
-      mx = fmaxf(mx, fabsf(xv[i]));
-      sm += fabsf(xv[i]);
+      mx = fmaxf(mx, fabsf(xv[c][i]));
+      sm += fabsf(xv[c][i]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1232,43 +1276,60 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
       sm += __shfl_xor_sync(0xffffffffu, sm, o);
     }
     if (lane == 0) {
-      xstat[0][warp] = mx;
-      xstat[1][warp] = sm;
+      xstat[c][0][warp] = mx;
+      xstat[c][1][warp] = sm;
     }
   }
   __syncthreads();
-  float xmax = 0.f, nx1 = 0.f;
+  float sx[kClips], nx1[kClips];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    xmax = fmaxf(xmax, xstat[0][i]);
-    nx1 += xstat[1][i];
-  }
-  nx1 *= 1.0001f;  // covers the fp32 rounding of the sum
-  const float sx = xmax > 0.f ? xmax / kXqMax : 0.f;
-  const float xinv = xmax > 0.f ? kXqMax / xmax : 0.f;
-  // B operand: row 0 = x_hi, row 1 = x_lo of xq = rint(x / sx) (|xq| <= 8191), one 8-row
-  // 128B-swizzled atom per 128-element K chunk (16-byte unit j of row n stored at unit j ^ n).
+  for (int c = 0; c < kClips; ++c) {
+    float xmax = 0.f, n1 = 0.f;
+    if (c < C) {
 #pragma unroll
-  for (int i = 0; i < 5; ++i) {
-    const int k = threadIdx.x + i * 256;
-    const int xq = max(-8191, min(8191, __float2int_rn(xv[i] * xinv)));
-    const int xh = (xq + 64) >> 7;  // floor((xq + 64) / 128), in [-64, 64]
-    const int xl = xq - (xh << 7);  // in [-64, 63]
-    const int c = k >> 7, kk = k & 127;
-    uint8_t* atom = xb + c * 8 * kQChunk;
-    atom[0 * kQChunk + ((((kk >> 4) ^ 0) & 7) << 4) + (kk & 15)] = static_cast<uint8_t>(static_cast<int8_t>(xh));
-    atom[1 * kQChunk + ((((kk >> 4) ^ 1) & 7) << 4) + (kk & 15)] = static_cast<uint8_t>(static_cast<int8_t>(xl));
+      for (int i = 0; i < 8; ++i) {
+        xmax = fmaxf(xmax, xstat[c][0][i]);
+        n1 += xstat[c][1][i];
+      }
+    }
+    nx1[c] = n1 * 1.0001f;  // covers the fp32 rounding of the sum
+    sx[c] = xmax > 0.f ? xmax / kXqMax : 0.f;
+    const float xinv = xmax > 0.f ? kXqMax / xmax : 0.f;
+    if (c >= C) continue;
+    // B operand: 16-byte unit j of row n of an 8-row 128B-swizzled atom is stored at unit j ^ (n % 8);
+    // rows 8..15 form the second atom of the K chunk.
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const int k = threadIdx.x + i * 256;
+      const int xq = max(-8191, min(8191, __float2int_rn(xv[c][i] * xinv)));
+      const int xh = (xq + 64) >> 7;  // floor((xq + 64) / 128), in [-64, 64]
+      const int xl = xq - (xh << 7);  // in [-64, 63]
+      const int ch = k >> 7, kk = k & 127;
+      uint8_t* chunk = xb + ch * S::kN * kQChunk;
+      const int n0 = 2 * c, n1r = 2 * c + 1;
+      chunk[(n0 >> 3) * 1024 + (n0 & 7) * kQChunk + ((((kk >> 4) ^ (n0 & 7)) & 7) << 4) + (kk & 15)] =
+          static_cast<uint8_t>(static_cast<int8_t>(xh));
+      chunk[(n1r >> 3) * 1024 + (n1r & 7) * kQChunk + ((((kk >> 4) ^ (n1r & 7)) & 7) << 4) + (kk & 15)] =
+          static_cast<uint8_t>(static_cast<int8_t>(xl));
+    }
   }
   fence_proxy_async_shared();  // B written by the generic proxy, read by the tensor core
   __syncthreads();
-  float xf[40];
-  load_x40(ys, xf);
 
-  const uint8_t* mask = msk[0];
-  if (kFinalize && p.first_mask && p.prompt_len > 0 && p.state[0] == p.prompt_len - 1) mask = msk[1];
+  const uint8_t* maskc[kClips];
+#pragma unroll
+  for (int c = 0; c < kClips; ++c) {
+    maskc[c] = msk[0];
+    if (kFinalize && c < C && p.first_mask && p.prompt_len > 0 && p.state[2 * c] == p.prompt_len - 1) maskc[c] = msk[1];
+  }
 
-  // ---- pass 1: int8 tensor-core GEMV, bounds per row ----
-  float lmax = -INFINITY, bmax = 0.f;
+  // ---- pass 1: int8 tensor-core GEMV, bounds per row and clip ----
+  float lmax[kClips], bmax[kClips];
+#pragma unroll
+  for (int c = 0; c < kClips; ++c) {
+    lmax[c] = -INFINITY;
+    bmax[c] = 0.f;
+  }
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t policy = policy_evict_first();
@@ -1283,7 +1344,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_s8(kQTileRows, 8);
+      constexpr uint32_t idesc = make_idesc_s8(kQTileRows, S::kN);
       const uint32_t xaddr = smem_u32(xb);
       bool ok = true;
       for (int t = 0; t < n_tiles && ok; ++t) {
@@ -1293,7 +1354,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(buf * 8);
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * S::kN);
         for (int c = 0; c < kQChunks; ++c) {
           const int it = t * kQChunks + c, s = it % kQStages;
           if (!mbar_wait(&full[s], (it / kQStages) & 1)) {
@@ -1303,7 +1364,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
           }
           tc_fence_after();
           const uint64_t adesc = sw128_desc(base + s * kQStageBytes);
-          const uint64_t bdesc = sw128_desc(xaddr + c * 8 * kQChunk);
+          const uint64_t bdesc = sw128_desc(xaddr + c * S::kN * kQChunk);
 #pragma unroll
           for (int kk = 0; kk < kQChunk / 32; ++kk)
             tc_mma_i8(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
@@ -1321,97 +1382,126 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
         break;
       }
       tc_fence_after();
-      uint32_t v0, v1;
-      tc_ld2(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 8), v0, v1);
+      uint32_t vv[kClips == 1 ? 2 : 16];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * S::kN);
+      if constexpr (kClips == 1) {
+        tc_ld2(taddr, vv[0], vv[1]);
+      } else {
+        tc_ld16(taddr, vv);
+      }
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       const int li = t * kQTileRows + q * 32 + lane;
       if (li < nrows) {
-        const int sum = 128 * static_cast<int>(v0) + static_cast<int>(v1);  // sum_i q_ri xq_i, exact
         const float4 prm = rps[li];
-        const float approx = prm.x * sx * static_cast<float>(sum);
-        const float b = (nx1 * prm.y + sx * prm.z + 4e-7f * fabsf(approx)) * 1.00001f + 1e-30f;
-        if (mask[li]) {
-          ub[li] = -INFINITY;
-        } else {
-          ub[li] = approx + b;
-          lmax = fmaxf(lmax, approx - b);
-          bmax = fmaxf(bmax, b);
-          if (!isfinite(approx) || !isfinite(b)) bmax = INFINITY;
-          // Rows that may survive the selection (against the lower bounds seen so far) have their
-          // fp16 row fetched into L2 now, so the exact pass reads them from L2. A hint only.
-          const float lo = approx - b;
-          const float run = fmaxf(ordered_to_float(atomicMax(&s_lo_max, float_to_ordered(lo))), lo);
-          if (approx + b >= run - (0x1p-9f * (fabsf(run) + 2.f * b) + 0x1p-23f))
-            l2_prefetch(p.w + static_cast<size_t>(r0 + li) * kHidden, kHidden * 2);
+        bool fetch = false;
+#pragma unroll
+        for (int c = 0; c < kClips; ++c) {
+          if (c >= C) break;
+          const int sum = 128 * static_cast<int>(vv[2 * c]) + static_cast<int>(vv[2 * c + 1]);  // exact
+          const float approx = prm.x * sx[c] * static_cast<float>(sum);
+          const float b = (nx1[c] * prm.y + sx[c] * prm.z + 4e-7f * fabsf(approx)) * 1.00001f + 1e-30f;
+          if (maskc[c][li]) {
+            ub[c * kLmMaxRowsPerCta + li] = -INFINITY;
+          } else {
+            ub[c * kLmMaxRowsPerCta + li] = approx + b;
+            lmax[c] = fmaxf(lmax[c], approx - b);
+            bmax[c] = fmaxf(bmax[c], b);
+            if (!isfinite(approx) || !isfinite(b)) bmax[c] = INFINITY;
+            // Rows that may survive the selection (against the lower bounds seen so far) have their
+            // fp16 row fetched into L2 now, so the exact pass reads them from L2. A hint only.
+            const float lo = approx - b;
+            const float run = fmaxf(ordered_to_float(atomicMax(&s_lo_max[c], float_to_ordered(lo))), lo);
+            if (approx + b >= run - (0x1p-9f * (fabsf(run) + 2.f * b) + 0x1p-23f)) fetch = true;
+          }
         }
+        if (fetch) l2_prefetch(p.w + static_cast<size_t>(r0 + li) * kHidden, kHidden * 2);
       }
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
-  }
-  if (lane == 0) {
-    warp_l[warp] = lmax;
-    warp_b[warp] = bmax;
+  for (int c = 0; c < kClips; ++c) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lmax[c] = fmaxf(lmax[c], __shfl_xor_sync(0xffffffffu, lmax[c], o));
+      bmax[c] = fmaxf(bmax[c], __shfl_xor_sync(0xffffffffu, bmax[c], o));
+    }
+    if (lane == 0) {
+      warp_l[c][warp] = lmax[c];
+      warp_b[c][warp] = bmax[c];
+    }
   }
   __syncthreads();
 
-  // ---- row selection: U_r >= T - m (every row when the bound is unusable) ----
-  float t = -INFINITY, bm = 0.f;
+  // ---- row selection per clip: U_r >= T - m (every row when the bound is unusable) ----
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    t = fmaxf(t, warp_l[i]);
-    bm = fmaxf(bm, warp_b[i]);
-  }
-  const bool all_rows = !(fabsf(t) < 32768.f) || !(bm < 32768.f);
-  const float thr = t - (0x1p-9f * (fabsf(t) + 2.f * bm) + 0x1p-23f);
-  for (int i = threadIdx.x; i < nrows; i += 256) {
-    if (!mask[i] && (all_rows || ub[i] >= thr)) cand[atomicAdd(&ncand, 1)] = static_cast<unsigned short>(i);
+  for (int c = 0; c < kClips; ++c) {
+    if (c >= C) break;
+    float t = -INFINITY, bm = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      t = fmaxf(t, warp_l[c][i]);
+      bm = fmaxf(bm, warp_b[c][i]);
+    }
+    const bool all_rows = !(fabsf(t) < 32768.f) || !(bm < 32768.f);
+    const float thr = t - (0x1p-9f * (fabsf(t) + 2.f * bm) + 0x1p-23f);
+    for (int i = threadIdx.x; i < nrows; i += 256) {
+      if (!maskc[c][i] && (all_rows || ub[c * kLmMaxRowsPerCta + i] >= thr))
+        cand[c * kLmMaxRowsPerCta + atomicAdd(&ncand[c], 1)] = static_cast<unsigned short>(i);
+    }
   }
   __syncthreads();
 
   // ---- pass 2: exact fp16 logits of the surviving rows, four rows per warp at a time ----
-  const int nc = ncand;
-  unsigned long long mine = 0;
-  for (int j = 4 * warp; j < nc; j += 32) {
-    int rr[4];
-    const half* rows[4];
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    float xf[40];
+    load_x40(ys + c * kHidden, xf);
+    const int nc = ncand[c];
+    const unsigned short* cl = cand + c * kLmMaxRowsPerCta;
+    unsigned long long mine = 0;
+    for (int j = 4 * warp; j < nc; j += 32) {
+      int rr[4];
+      const half* rows[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      rr[q] = r0 + cand[min(j + q, nc - 1)];  // a repeated row repeats its key
-      rows[q] = p.w + static_cast<size_t>(rr[q]) * kHidden;
-    }
-    float acc[4];
-    dot1280_ptrs<4>(rows, xf, acc);
+      for (int q = 0; q < 4; ++q) {
+        rr[q] = r0 + cl[min(j + q, nc - 1)];  // a repeated row repeats its key
+        rows[q] = p.w + static_cast<size_t>(rr[q]) * kHidden;
+      }
+      float acc[4];
+      dot1280_ptrs<4>(rows, xf, acc);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const unsigned long long k = pack_score(round_half(acc[q]), rr[q]);
-      mine = k > mine ? k : mine;
+      for (int q = 0; q < 4; ++q) {
+        const unsigned long long k = pack_score(round_half(acc[q]), rr[q]);
+        mine = k > mine ? k : mine;
+      }
     }
+    if (lane == 0) warp_best[c][warp] = mine;
   }
-  if (lane == 0) warp_best[warp] = mine;
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 32);
+    tmem_dealloc(tmem, S::kTmemCols);
   }
   if (threadIdx.x == 0) {
-    unsigned long long m = 0;
-    for (int i = 0; i < 8; ++i) m = warp_best[i] > m ? warp_best[i] : m;
-    if (m) atomicMax(p.best, m);
+    for (int c = 0; c < C; ++c) {
+      unsigned long long m = 0;
+      for (int i = 0; i < 8; ++i) m = warp_best[c][i] > m ? warp_best[c][i] : m;
+      if (m) atomicMax(p.best + c, m);
+    }
     if (kFinalize) {
       __threadfence();
       const unsigned prev = atomicAdd(p.counter, 1u);
       if (prev == gridDim.x - 1) {
         __threadfence();
-        const unsigned long long b = atomicExch(p.best, 0ull);
-        finalize_token(b, p.tokens, p.n_tokens, p.state, p.cur, p.max_pos, p.prompt_len);
+        for (int c = 0; c < C; ++c) {
+          const unsigned long long b = atomicExch(p.best + c, 0ull);
+          finalize_token(b, p.tokens + c * p.tokens_stride, p.n_tokens, p.state + 2 * c, p.cur + c, p.max_pos,
+                         p.prompt_len);
+        }
         *p.counter = 0u;
       }
     }
@@ -1758,6 +1848,362 @@ __global__ void argmax_index_kernel(unsigned long long* key, int64_t* out_index)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Batched decode: one decode step for `clips` independent clips (at most kMaxClips) per weight read.
+// Each clip has its own residual stream, caches, position and tokens; the weights are streamed once
+// per step for all of them. Every per-clip value is computed with exactly the arithmetic of the
+// batch-1 step above (the same LayerNorm summation order, the same per-lane dot-product chains and
+// warp xor-trees, the same split attention and combine, the same head-ordered output-projection
+// sum, the same LM-head key), so each clip's tokens are bit-identical to decoding it alone.
+constexpr int kMaxClips = 8;
+
+struct BatchGemvParams {
+  const half* w;  // [n_out, 1280]
+  const half* b;  // [n_out] or null
+  half* out;      // clip c's outputs at out + c * out_stride
+  int n_out, out_stride, clips;
+  const half* h;  // [clips, 1280] LayerNorm input
+  const half* gamma;
+  const half* beta;
+  float eps;
+  // layer 0: h_c = fp16(embed[token_c] + pos_embed[position_c]), written to h_out by CTA 0
+  const half* embed;
+  const half* pos_embed;
+  const int64_t* cur;    // [clips]
+  const int64_t* state;  // [clips, 2]
+  const int64_t* prompt;
+  int prompt_len, vocab, max_pos;
+  half* h_out;
+};
+
+// LayerNorm (+ optional GELU epilogue) GEMV for every clip: out_c[r] = act(W[r] . LN(h_c) + b[r]).
+// The CTA's 8 * kRowsPerWarp weight rows are bulk-copied into shared memory before the PDL wait;
+// the LayerNorm rows of all clips are kept in shared memory as fp32 (exact fp16 values). Warp w
+// owns rows w, w + 8, ...: per 16-byte weight chunk it loads the chunk of each of its rows once and
+// runs every clip's fma chain (the lane order of dot1280_lane) from one read of that clip's x chunk.
+template <int kAct, int kRowsPerWarp, bool kEmbed>
+__global__ void __launch_bounds__(256) bln_gemv_kernel(BatchGemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float red[kMaxClips][16];
+  constexpr int kRows = 8 * kRowsPerWarp;
+  half* ws = reinterpret_cast<half*>(smem);
+  float* xs = reinterpret_cast<float*>(smem + kRows * kHidden * 2);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = blockIdx.x * kRows;
+  const int nr = min(kRows, p.n_out - r0);
+  const int C = p.clips;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    if (nr > 0) {
+      mbar_arrive_expect_tx(&bar, static_cast<unsigned>(nr) * kHidden * 2);
+      const uint64_t pol = policy_evict_first();
+      for (int r = 0; r < nr; ++r)
+        bulk_g2s_stream(ws + r * kHidden, p.w + static_cast<size_t>(r0 + r) * kHidden, kHidden * 2, &bar, pol);
+    }
+  }
+  float g[5], be[5], bias[kRowsPerWarp];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    g[i] = __half2float(p.gamma[tid + i * 256]);
+    be[i] = __half2float(p.beta[tid + i * 256]);
+  }
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int r = warp + 8 * i;
+    bias[i] = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+
+  // LayerNorm of every clip (ln1280_stats order: per-thread sums, warp xor-tree, warps in order)
+  float v[kMaxClips][5];
+#pragma unroll
+  for (int c = 0; c < kMaxClips; ++c) {
+    if (c >= C) break;
+    if (kEmbed) {
+      const int64_t raw = p.state[2 * c];
+      const int pos = static_cast<int>(min(max(raw, int64_t(0)), int64_t(p.max_pos - 1)));
+      int64_t tok = pos < p.prompt_len ? p.prompt[pos] : p.cur[c];
+      if (raw < 0 || raw >= p.max_pos || tok < 0 || tok >= p.vocab) {
+        if (tid == 0 && blockIdx.x == 0) flag_error(FW_DEVERR_BAD_INDEX);
+        tok = tok < 0 ? 0 : (tok >= p.vocab ? p.vocab - 1 : tok);
+      }
+      const half* er = p.embed + static_cast<size_t>(tok) * kHidden;
+      const half* pr = p.pos_embed + static_cast<size_t>(pos) * kHidden;
+#pragma unroll
+      for (int i = 0; i < 5; ++i) {
+        v[c][i] = round_half(__half2float(er[tid + i * 256]) + __half2float(pr[tid + i * 256]));
+        if (blockIdx.x == 0) p.h_out[c * kHidden + tid + i * 256] = __float2half(v[c][i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 5; ++i) v[c][i] = __half2float(p.h[c * kHidden + tid + i * 256]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) sum += v[c][i];
+    sum = warp_sum(sum);
+    if (lane == 0) red[c][warp] = sum;
+  }
+  __syncthreads();
+  float mean[kMaxClips];
+#pragma unroll
+  for (int c = 0; c < kMaxClips; ++c) {
+    if (c >= C) break;
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m += red[c][i];
+    m /= static_cast<float>(kHidden);
+    mean[c] = m;
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const float d = v[c][i] - m;
+      sq = fmaf(d, d, sq);
+    }
+    sq = warp_sum(sq);
+    if (lane == 0) red[c][8 + warp] = sq;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < kMaxClips; ++c) {
+    if (c >= C) break;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) var += red[c][8 + i];
+    const float inv = rsqrtf(var / static_cast<float>(kHidden) + p.eps);
+#pragma unroll
+    for (int i = 0; i < 5; ++i)
+      xs[c * kHidden + tid + i * 256] = __half2float(__float2half(ln_apply(v[c][i], mean[c], inv, g[i], be[i])));
+  }
+  __syncthreads();
+  if (nr > 0 && !mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
+
+  float acc[kRowsPerWarp][kMaxClips];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int c = 0; c < kMaxClips; ++c) acc[i][c] = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < 5; ++ch) {
+    uint4 wv[kRowsPerWarp];
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i)
+      wv[i] = reinterpret_cast<const uint4*>(ws + (warp + 8 * i) * kHidden)[lane + 32 * ch];
+#pragma unroll
+    for (int c = 0; c < kMaxClips; ++c) {
+      if (c >= C) break;
+      const float4* xp = reinterpret_cast<const float4*>(xs + c * kHidden + (lane + 32 * ch) * 8);
+      const float4 xa = xp[0], xb = xp[1];
+      const float x8[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i) {
+        const half2* h2 = reinterpret_cast<const half2*>(&wv[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(h2[k]);
+          acc[i][c] = fmaf(f.x, x8[2 * k], acc[i][c]);
+          acc[i][c] = fmaf(f.y, x8[2 * k + 1], acc[i][c]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int r = warp + 8 * i;
+#pragma unroll
+    for (int c = 0; c < kMaxClips; ++c) {
+      if (c >= C) break;
+      const float a = warp_sum(acc[i][c]);
+      if (lane == c && r < nr) {
+        float o = round_half(a + bias[i]);
+        if (kAct == 1) o = gelu_erf(o);
+        p.out[static_cast<size_t>(c) * p.out_stride + r0 + r] = __float2half(o);
+      }
+    }
+  }
+}
+
+// Output projection of the attention heads + bias + residual for every clip:
+// h_c[r] = fp16(h_c[r] + fp16(sum_head (W_o[head][r] . o_c[head]) + b[r])) with W_o head-major
+// [heads, 1280, 64]. Per (row, head) the dot is the two-chain rotated-chunk order of
+// head_block_kernel's output-projection partial and the head sum runs in head order, so the result
+// equals head_block_kernel's. The CTA's kOutRowsB rows of every head are bulk-copied into shared
+// memory before the PDL wait. Thread (row, clip, group) computes the partials of kHeadsPerGroup heads.
+constexpr int kOutRowsB = 10;      // 1280 / 10 = 128 CTAs
+constexpr int kHeadsPerGroup = 5;  // 20 heads = 4 groups
+constexpr int kOutThreadsB = kOutRowsB * kMaxClips * (kHeads / kHeadsPerGroup);  // 320
+
+struct BatchOutParams {
+  const half* wo;    // head-major [heads, 1280, 64]
+  const half* bo;    // [1280]
+  const half* attn;  // [clips, 1280] attention outputs (head-major within a clip)
+  half* h;           // [clips, 1280] residual stream, updated in place
+  int clips;
+};
+
+constexpr int kBoutSmem = kHeads * kOutRowsB * kHeadDim * 2 + kMaxClips * kHidden * 4;  // 25.6 KB + 40 KB
+
+__global__ void __launch_bounds__(kOutThreadsB) bout_residual_kernel(BatchOutParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  auto ws = reinterpret_cast<half (*)[kOutRowsB][kHeadDim]>(smem);                           // [heads][rows][64]
+  auto os = reinterpret_cast<float (*)[kHidden]>(smem + kHeads * kOutRowsB * kHeadDim * 2);  // [clips][1280]
+  __shared__ float part[kOutRowsB][kMaxClips][kHeads];
+  __shared__ __align__(8) uint64_t bar;
+  const int tid = threadIdx.x;
+  const int r0 = blockIdx.x * kOutRowsB;
+  const int C = p.clips;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(&bar, kHeads * kOutRowsB * kHeadDim * 2);
+    const uint64_t pol = policy_evict_first();
+    for (int hh = 0; hh < kHeads; ++hh)
+      bulk_g2s_stream(&ws[hh][0][0], p.wo + (static_cast<size_t>(hh) * kHidden + r0) * kHeadDim,
+                      kOutRowsB * kHeadDim * 2, &bar, pol);
+  }
+  const int rl = tid % kOutRowsB, c = (tid / kOutRowsB) % kMaxClips, grp = tid / (kOutRowsB * kMaxClips);
+  const int r = r0 + rl;
+  const float obias = p.bo ? __half2float(p.bo[r]) : 0.f;
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  for (int i = tid; i < C * kHidden; i += kOutThreadsB) os[i / kHidden][i % kHidden] = __half2float(p.attn[i]);
+  __syncthreads();
+  if (!mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
+  if (c < C) {
+#pragma unroll
+    for (int q = 0; q < kHeadsPerGroup; ++q) {
+      const int hh = grp * kHeadsPerGroup + q;
+      const uint4* wr = reinterpret_cast<const uint4*>(&ws[hh][rl][0]);
+      const float4* o4 = reinterpret_cast<const float4*>(&os[c][hh * kHeadDim]);
+      float acc2[2] = {0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int ch = (j + r) & 7;  // head_block_kernel's rotation (its row index mod 8 equals r's)
+        const uint4 wv = wr[ch];
+        const float4 oa = o4[2 * ch], ob = o4[2 * ch + 1];
+        const half2* w2 = reinterpret_cast<const half2*>(&wv);
+        const float2 f0 = __half22float2(w2[0]), f1 = __half22float2(w2[1]);
+        const float2 f2 = __half22float2(w2[2]), f3 = __half22float2(w2[3]);
+        float& a = acc2[j & 1];
+        a = fmaf(f0.x, oa.x, a);
+        a = fmaf(f0.y, oa.y, a);
+        a = fmaf(f1.x, oa.z, a);
+        a = fmaf(f1.y, oa.w, a);
+        a = fmaf(f2.x, ob.x, a);
+        a = fmaf(f2.y, ob.y, a);
+        a = fmaf(f3.x, ob.z, a);
+        a = fmaf(f3.y, ob.w, a);
+      }
+      part[rl][c][hh] = acc2[0] + acc2[1];
+    }
+  }
+  __syncthreads();
+  if (grp == 0 && c < C) {
+    float acc = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < kHeads; ++hh) acc += part[rl][c][hh];
+    half* hr = p.h + static_cast<size_t>(c) * kHidden + r;
+    *hr = __float2half(__half2float(*hr) + round_half(acc + obias));
+  }
+}
+
+// fc2 + residual for every clip: h_c[r] = fp16(h_c[r] + fp16(W[r] . x_c + b[r])), x_c = the fc1 output
+// [5120] of clip c. Same K split and reduction order as gemv_residual_kernel<20> (thread t owns
+// 16-byte chunks t and t + 320 of every row, warp xor-tree, warps summed in order), with each weight
+// chunk read from shared memory once for all clips.
+constexpr int kBfc2Threads = kResidThreads;  // 320
+
+struct BatchFc2Params {
+  const half* w;   // [1280, 5120]
+  const half* b;   // [1280]
+  const half* x;   // [clips, 5120]
+  half* h;         // [clips, 1280]
+  int clips;
+};
+
+__global__ void __launch_bounds__(kBfc2Threads) bfc2_residual_kernel(BatchFc2Params p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float red[kBfc2Threads / 32][kResidRows][kMaxClips];
+  constexpr int kc = kFfn / 8;                           // 640 chunks per row
+  constexpr int kPer = (kc + kBfc2Threads - 1) / kBfc2Threads;  // 2
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = blockIdx.x * kResidRows;
+  const int C = p.clips;
+  const uint4* ws = reinterpret_cast<const uint4*>(smem);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(&bar, kResidRows * kFfn * 2);
+    const uint64_t pol = policy_evict_first();
+    for (int r = 0; r < kResidRows; ++r)
+      bulk_g2s_stream(smem + static_cast<size_t>(r) * kFfn * 2, p.w + static_cast<size_t>(r0 + r) * kFfn, kFfn * 2,
+                      &bar, pol);
+  }
+  const int orow = tid % kResidRows, oc = tid / kResidRows;  // owner of (row, clip) for the epilogue
+  const bool owner = oc < C;
+  const float bias = (p.b && owner) ? __half2float(p.b[r0 + orow]) : 0.f;
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  uint4 xv[kMaxClips][kPer];
+#pragma unroll
+  for (int c = 0; c < kMaxClips; ++c) {
+    if (c >= C) break;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int ch = tid + kBfc2Threads * j;
+      xv[c][j] = ch < kc ? reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(c) * kFfn)[ch]
+                         : make_uint4(0, 0, 0, 0);
+    }
+  }
+  const float hres = owner ? __half2float(p.h[static_cast<size_t>(oc) * kHidden + r0 + orow]) : 0.f;
+  if (!mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
+#pragma unroll 1
+  for (int r = 0; r < kResidRows; ++r) {
+    float acc[kMaxClips];
+#pragma unroll
+    for (int c = 0; c < kMaxClips; ++c) acc[c] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int ch = tid + kBfc2Threads * j;
+      if (ch < kc) {
+        const uint4 wv = ws[r * kc + ch];
+        const half2* pw = reinterpret_cast<const half2*>(&wv);
+#pragma unroll
+        for (int c = 0; c < kMaxClips; ++c) {
+          if (c >= C) break;
+          const half2* px = reinterpret_cast<const half2*>(&xv[c][j]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fw = __half22float2(pw[e]), fx = __half22float2(px[e]);
+            acc[c] = fmaf(fw.x, fx.x, acc[c]);
+            acc[c] = fmaf(fw.y, fx.y, acc[c]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kMaxClips; ++c) {
+      if (c >= C) break;
+      const float a = warp_sum(acc[c]);
+      if (lane == 0) red[warp][r][c] = a;
+    }
+  }
+  __syncthreads();
+  if (owner) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kBfc2Threads / 32; ++w) sum += red[w][orow][oc];
+    p.h[static_cast<size_t>(oc) * kHidden + r0 + orow] = __float2half(hres + round_half(sum + bias));
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host launchers.
 constexpr int kQkvRows = 24;   // 3840 / 24 = 160 CTAs
 constexpr int kFc1Rows = 32;   // 5120 / 32 = 160 CTAs
@@ -1853,9 +2299,10 @@ static int make_lm_map(CUtensorMap* m, const void* wq, int vocab) {
   return FW_OK;
 }
 
-template <bool kLN, bool kFinalize>
+template <bool kLN, bool kFinalize, int kClips = 1>
 static int launch_lm_head_q(LmParams p, cudaStream_t s, bool pdl) {
-  auto kern = lm_head_q_kernel<kLN, kFinalize>;
+  auto kern = lm_head_q_kernel<kLN, kFinalize, kClips>;
+  constexpr int smem = LmqShape<kClips>::kSmem;
   const int grid = num_sms();
   p.rows_per_cta = (p.vocab + grid - 1) / grid;
   if (p.rows_per_cta > kLmMaxRowsPerCta)
@@ -1863,9 +2310,32 @@ static int launch_lm_head_q(LmParams p, cudaStream_t s, bool pdl) {
   CUtensorMap map;
   int rc = make_lm_map(&map, p.wq, p.vocab);
   if (rc) return rc;
-  cudaError_t e = ensure_smem(kern, kQSmem);
-  if (e == cudaSuccess) e = launch(kern, dim3(grid), dim3(256), kQSmem, s, pdl, map, p);
+  cudaError_t e = ensure_smem(kern, smem);
+  if (e == cudaSuccess) e = launch(kern, dim3(grid), dim3(256), smem, s, pdl, map, p);
   return launch_status(e, "lm_head_argmax_q");
+}
+
+template <int kAct, int kRowsPerWarp, bool kEmbed>
+static int launch_bln_gemv(const BatchGemvParams& p, cudaStream_t s) {
+  auto kern = bln_gemv_kernel<kAct, kRowsPerWarp, kEmbed>;
+  constexpr int rows = 8 * kRowsPerWarp;
+  const int smem = rows * kHidden * 2 + p.clips * kHidden * 4;
+  cudaError_t e = ensure_smem(kern, rows * kHidden * 2 + kMaxClips * kHidden * 4);
+  if (e == cudaSuccess) e = launch(kern, dim3((p.n_out + rows - 1) / rows), dim3(256), smem, s, true, p);
+  return launch_status(e, "batch_ln_gemv");
+}
+
+static int launch_bout(const BatchOutParams& p, cudaStream_t s) {
+  cudaError_t e = ensure_smem(bout_residual_kernel, kBoutSmem);
+  if (e == cudaSuccess) e = launch(bout_residual_kernel, dim3(kHidden / kOutRowsB), dim3(kOutThreadsB), kBoutSmem, s, true, p);
+  return launch_status(e, "batch_out_proj");
+}
+
+static int launch_bfc2(const BatchFc2Params& p, cudaStream_t s) {
+  constexpr int smem = kResidRows * kFfn * 2;
+  cudaError_t e = ensure_smem(bfc2_residual_kernel, smem);
+  if (e == cudaSuccess) e = launch(bfc2_residual_kernel, dim3(kHidden / kResidRows), dim3(kBfc2Threads), smem, s, true, p);
+  return launch_status(e, "batch_fc2");
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -2335,6 +2805,157 @@ int fw_decoder_step_trace(const fw_decoder_t* d, void* trace, fw_stream_t stream
   FW_REQUIRE(trace != nullptr, FW_ERR_NULL, "decoder_step_trace: trace is NULL");
   FW_REQUIRE(aligned16(trace), FW_ERR_ALIGN, "decoder_step_trace: trace must be 16-byte aligned");
   return decoder_one_step(d, static_cast<cudaStream_t>(stream), static_cast<half*>(trace));
+}
+
+int fw_batch_decoder_step(const fw_batch_decoder_t* d, int steps, fw_stream_t stream) {
+  FW_REQUIRE(d != nullptr, FW_ERR_NULL, "batch_decoder_step: descriptor is NULL");
+  FW_REQUIRE(d->clips > 0 && d->clips <= kMaxClips, FW_ERR_SHAPE, "batch_decoder_step: clips must be 1..%d",
+             kMaxClips);
+  FW_REQUIRE(d->n_layers > 0 && d->n_layers <= FW_MAX_LAYERS, FW_ERR_SHAPE, "batch_decoder_step: bad layer count");
+  FW_REQUIRE(d->heads * kHeadDim == kHidden, FW_ERR_SHAPE, "batch_decoder_step: heads * 64 must be %d", kHidden);
+  FW_REQUIRE(d->max_pos > 0 && d->enc_len > 0 && d->vocab > 0 && d->n_tokens > 0, FW_ERR_SHAPE,
+             "batch_decoder_step: bad sizes");
+  FW_REQUIRE(d->max_pos <= kMaxSplits * kSplitKeys && d->enc_len <= kMaxSplits * kSplitKeys, FW_ERR_SHAPE,
+             "batch_decoder_step: max_pos and enc_len must be <= %d", kMaxSplits * kSplitKeys);
+  FW_REQUIRE(d->embed && d->pos_embed && d->lm_head && d->final_g && d->final_b && d->h && d->qkv && d->attn &&
+                 d->ffn && d->part_m && d->part_l && d->part_acc && d->counters && d->cur && d->state && d->tokens &&
+                 d->best && d->lm_q && d->lm_rp,
+             FW_ERR_NULL, "batch_decoder_step: a required pointer is NULL");
+  FW_REQUIRE(d->prompt_len == 0 || d->prompt != nullptr, FW_ERR_NULL, "batch_decoder_step: prompt is NULL");
+  const int self_splits = (d->max_pos + kSplitKeys - 1) / kSplitKeys;
+  const int cross_splits = (d->enc_len + kSplitKeys - 1) / kSplitKeys;
+  FW_REQUIRE(d->ws_splits >= self_splits && d->ws_splits >= cross_splits, FW_ERR_SHAPE,
+             "batch_decoder_step: ws_splits must be >= %d", self_splits > cross_splits ? self_splits : cross_splits);
+  FW_REQUIRE(d->self_clip_stride % 8 == 0 && d->cross_clip_stride % 8 == 0 && aligned16(d->lm_q) &&
+                 aligned16(d->lm_rp) && aligned16(d->h) && aligned16(d->qkv) && aligned16(d->attn) && aligned16(d->ffn),
+             FW_ERR_ALIGN, "batch_decoder_step: buffers and clip strides must be 16-byte aligned");
+  for (int l = 0; l < d->n_layers; ++l) {
+    const fw_decoder_layer_t& L = d->layers[l];
+    FW_REQUIRE(L.self_k && L.self_v && L.cross_k && L.cross_v && L.qkv_w && L.out_w && L.cq_w && L.co_w && L.fc1_w &&
+                   L.fc2_w && L.ln1_g && L.ln1_b && L.ln2_g && L.ln2_b && L.ln3_g && L.ln3_b,
+               FW_ERR_NULL, "batch_decoder_step: layer %d is missing a weight or cache pointer", l);
+    FW_REQUIRE(aligned16(L.self_k) && aligned16(L.self_v) && aligned16(L.cross_k) && aligned16(L.cross_v),
+               FW_ERR_ALIGN, "batch_decoder_step: caches must be 16-byte aligned");
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int C = d->clips;
+  half* h = static_cast<half*>(d->h);
+  half* qkv = static_cast<half*>(d->qkv);
+  half* attn = static_cast<half*>(d->attn);
+  half* ffn = static_cast<half*>(d->ffn);
+  for (int step = 0; step < steps; ++step) {
+    for (int l = 0; l < d->n_layers; ++l) {
+      const fw_decoder_layer_t& L = d->layers[l];
+      int rc;
+      BatchGemvParams g{};
+      g.clips = C;
+      g.h = h;
+      g.eps = d->eps;
+      // LN1 + q/k/v (layer 0: h from the token embedding and position)
+      g.w = static_cast<const half*>(L.qkv_w);
+      g.b = static_cast<const half*>(L.qkv_b);
+      g.out = qkv;
+      g.n_out = 3 * kHidden;
+      g.out_stride = 3 * kHidden;
+      g.gamma = static_cast<const half*>(L.ln1_g);
+      g.beta = static_cast<const half*>(L.ln1_b);
+      g.embed = static_cast<const half*>(d->embed);
+      g.pos_embed = static_cast<const half*>(d->pos_embed);
+      g.cur = d->cur;
+      g.state = d->state;
+      g.prompt = d->prompt;
+      g.prompt_len = d->prompt_len;
+      g.vocab = d->vocab;
+      g.max_pos = d->max_pos;
+      g.h_out = h;
+      rc = l == 0 ? launch_bln_gemv<0, 3, true>(g, s) : launch_bln_gemv<0, 3, false>(g, s);
+      if (rc) return rc;
+      // self attention over position + 1 keys with the cache write, split combine fused
+      AttnParams a{};
+      a.q = qkv;
+      a.k = static_cast<half*>(L.self_k);
+      a.v = static_cast<half*>(L.self_v);
+      a.k_new = qkv + kHidden;
+      a.v_new = qkv + 2 * kHidden;
+      a.len_state = d->state;
+      a.max_len = d->max_pos;
+      a.scale = d->scale;
+      a.part_m = d->part_m;
+      a.part_l = d->part_l;
+      a.part_acc = d->part_acc;
+      a.out = attn;
+      a.counters = d->counters;
+      a.clip_q = 3 * kHidden;
+      a.clip_kv = d->self_clip_stride;
+      a.clip_new = 3 * kHidden;
+      a.clip_out = kHidden;
+      a.clip_state = 2;
+      cudaError_t e = launch(attn_split_kernel, dim3(d->heads, self_splits, C), dim3(64), 0, s, true, a);
+      if ((rc = launch_status(e, "batch_self_attention"))) return rc;
+      BatchOutParams o{static_cast<const half*>(L.out_w), static_cast<const half*>(L.out_b), attn, h, C};
+      if ((rc = launch_bout(o, s))) return rc;
+      // LN2 + cross q (into the q slot of qkv), cross attention, cross out_proj + residual
+      g.w = static_cast<const half*>(L.cq_w);
+      g.b = static_cast<const half*>(L.cq_b);
+      g.n_out = kHidden;
+      g.gamma = static_cast<const half*>(L.ln2_g);
+      g.beta = static_cast<const half*>(L.ln2_b);
+      if ((rc = launch_bln_gemv<0, 1, false>(g, s))) return rc;
+      AttnParams x{};
+      x.q = qkv;
+      x.k = const_cast<half*>(static_cast<const half*>(L.cross_k));
+      x.v = const_cast<half*>(static_cast<const half*>(L.cross_v));
+      x.max_len = d->enc_len;
+      x.scale = d->scale;
+      x.part_m = d->part_m;
+      x.part_l = d->part_l;
+      x.part_acc = d->part_acc;
+      x.out = attn;
+      x.counters = d->counters;
+      x.clip_q = 3 * kHidden;
+      x.clip_kv = d->cross_clip_stride;
+      x.clip_out = kHidden;
+      e = launch(attn_split_kernel, dim3(d->heads, cross_splits, C), dim3(64), 0, s, true, x);
+      if ((rc = launch_status(e, "batch_cross_attention"))) return rc;
+      BatchOutParams co{static_cast<const half*>(L.co_w), static_cast<const half*>(L.co_b), attn, h, C};
+      if ((rc = launch_bout(co, s))) return rc;
+      // LN3 + fc1 + GELU, fc2 + residual
+      g.w = static_cast<const half*>(L.fc1_w);
+      g.b = static_cast<const half*>(L.fc1_b);
+      g.out = ffn;
+      g.n_out = kFfn;
+      g.out_stride = kFfn;
+      g.gamma = static_cast<const half*>(L.ln3_g);
+      g.beta = static_cast<const half*>(L.ln3_b);
+      if ((rc = launch_bln_gemv<1, 4, false>(g, s))) return rc;
+      BatchFc2Params f{static_cast<const half*>(L.fc2_w), static_cast<const half*>(L.fc2_b), ffn, h, C};
+      if ((rc = launch_bfc2(f, s))) return rc;
+    }
+    LmParams m{};
+    m.h = h;
+    m.gamma = static_cast<const half*>(d->final_g);
+    m.beta = static_cast<const half*>(d->final_b);
+    m.eps = d->eps;
+    m.w = static_cast<const half*>(d->lm_head);
+    m.wq = static_cast<const int8_t*>(d->lm_q);
+    m.rp = static_cast<const float4*>(d->lm_rp);
+    m.vocab = d->vocab;
+    m.mask = d->base_mask;
+    m.first_mask = d->first_mask;
+    m.best = reinterpret_cast<unsigned long long*>(d->best);
+    m.counter = d->counters + C * d->heads;
+    m.tokens = d->tokens;
+    m.n_tokens = d->n_tokens;
+    m.tokens_stride = d->n_tokens;
+    m.state = d->state;
+    m.cur = d->cur;
+    m.max_pos = d->max_pos;
+    m.prompt_len = d->prompt_len;
+    m.clips = C;
+    int rc = launch_lm_head_q<true, true, kMaxClips>(m, s, true);
+    if (rc) return rc;
+  }
+  return FW_OK;
 }
 
 }  // extern "C"

@@ -89,6 +89,25 @@ class Ext:
                   _ptr(v_new), _ptr(part_m), part_m.numel(), _ptr(part_l), part_l.numel(), _ptr(part_acc),
                   part_acc.numel(), heads, max_len, float(scale), _stream())
 
+    def decode_attention_noalloc(self, q, k, v, out, len_state, k_new, v_new, scale):
+        """decode_attention without a workspace: the split partials live in the library's fixed device
+        array (heads * ceil(max_len / 64) <= 2048; calls that overlap on the GPU race on it)."""
+        for t, n in ((q, 'q'), (k, 'k'), (v, 'v'), (out, 'out')):
+            _check_half(t, n)
+        _check(k.dim() == 3 and k.size(2) == HEAD_DIM and k.shape == v.shape, 'k, v must be [heads, max_len, 64]')
+        heads, max_len = k.size(0), k.size(1)
+        _check(q.numel() == heads * HEAD_DIM and out.numel() == heads * HEAD_DIM, 'q, out must be [heads * 64]')
+        _check((k_new is None) == (v_new is None) == (len_state is None),
+               'len_state, k_new and v_new must be given together')
+        if k_new is not None:
+            _check_half(k_new, 'k_new')
+            _check_half(v_new, 'v_new')
+            _check(k_new.numel() == heads * HEAD_DIM and v_new.numel() == heads * HEAD_DIM,
+                   'k_new, v_new must be [heads, 64]')
+            _check(len_state.is_cuda and len_state.dtype == torch.long, 'len_state must be CUDA int64')
+        _lib.call('fw_decode_attention_noalloc', _ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(len_state), _ptr(k_new),
+                  _ptr(v_new), heads, max_len, float(scale), _stream())
+
     def lm_head_argmax(self, h, w, suppress, best):
         """best <- max(best, packed key of the unsuppressed argmax of fp16(w @ h))."""
         _check_half(h, 'h')
@@ -244,6 +263,10 @@ class Ext:
 
     def decoder_step(self, desc, steps=1):
         _lib.call('fw_decoder_step', ctypes.byref(desc), int(steps), _stream())
+
+    def batch_decoder_step(self, desc, steps=1):
+        """`steps` decode steps of every clip of a batched decoder descriptor (_lib.BatchDecoder)."""
+        _lib.call('fw_batch_decoder_step', ctypes.byref(desc), int(steps), _stream())
 
     def decoder_launch(self, desc, layer, block):
         """One launch of the decode step (block 0 self, 1 cross, 2 fc1, 3 fc2, 4 LM head)."""

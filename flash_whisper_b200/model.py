@@ -313,12 +313,93 @@ class CustomModel:
         self.run_steps(max(0, n_tokens - 1))
 
     # ---- public API --------------------------------------------------------------------------
-    @torch.inference_mode()
-    def transcribe(self, audio, max_new_tokens=None, stop_at_eos=True):
+    @staticmethod
+    def _check_audio(audio):
+        """custom/model.py:175-178."""
         if not isinstance(audio, np.ndarray) or audio.dtype != np.float32 or audio.ndim != 1:
             raise ValueError('audio must be a one-dimensional float32 NumPy array')
         if not 0 < audio.size <= N_SAMPLES or not np.isfinite(audio).all():
             raise ValueError('audio must contain finite samples and be between 0 and 30 seconds')
+
+    def batch_decoder(self):
+        """The batched decoder (flash_whisper_b200.batch.BatchDecoder, 8 clips), created on first use."""
+        if getattr(self, '_batch', None) is None:
+            from .batch import BatchDecoder
+            self._batch = BatchDecoder(self)
+            self.waves_host = torch.zeros(self._batch.clips, N_SAMPLES, dtype=torch.float32).pin_memory()
+        return self._batch
+
+    @torch.inference_mode()
+    def transcribe_batch(self, audios, max_new_tokens=None, stop_at_eos=True):
+        """Transcribes several clips, up to 8 per decoder weight read (flash_whisper_b200.batch).
+
+        Returns one dict per clip with transcribe()'s keys; each clip's token ids are exactly those
+        transcribe() returns for it alone. `max_new_tokens` is one limit or one per clip. Clips are
+        taken in the given order, 8 at a time; the stage times of a clip are those of its pass
+        (log-mel and encoder of every clip of the pass, then their joint decode)."""
+        for a in audios:
+            self._check_audio(a)
+        n_all = len(audios)
+        if isinstance(max_new_tokens, (list, tuple)):
+            limits = [min(int(x), self.max_new) for x in max_new_tokens]
+        else:
+            limits = [self.max_new if max_new_tokens is None else min(int(max_new_tokens), self.max_new)] * n_all
+        bd = self.batch_decoder()
+        stream = torch.cuda.current_stream()
+        results = []
+        for g0 in range(0, n_all, bd.clips):
+            group, lim = audios[g0:g0 + bd.clips], limits[g0:g0 + bd.clips]
+            n, steps = len(group), max(lim)
+            torch.cuda.synchronize()
+            start = time.perf_counter()
+            hw = self.waves_host.numpy()
+            for c, a in enumerate(group):
+                hw[c, :a.size] = a
+                hw[c, a.size:] = 0.0
+            ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+            for c in range(n):
+                ev[c][0].record(stream)
+                self.wave.copy_(self.waves_host[c], non_blocking=True)
+                self.run_mel()
+                ev[c][1].record(stream)
+                bd.encoder_slot(c)
+                ev[c][2].record(stream)
+            if steps - 1 >= bd.chunk:
+                bd._chunk_graph(n)
+            bd.prompt(n)
+            first_done = torch.cuda.Event()
+            first_done.record(stream)
+            first_done.synchronize()
+            ttft = time.perf_counter() - start
+            done = 1
+            while done < steps:
+                k = min(bd.chunk, steps - done)
+                bd.steps(n, k)
+                done += k
+                if stop_at_eos:
+                    toks = bd.tokens[:n, :done].cpu().tolist()
+                    if all(any(t in self.eos for t in row[:lim[c]]) or done >= lim[c] for c, row in enumerate(toks)):
+                        break
+            toks = bd.tokens[:n, :done].cpu().tolist()
+            ttlt = time.perf_counter() - start
+            mel_s = [e[0].elapsed_time(e[1]) / 1e3 for e in ev]
+            enc_s = [e[1].elapsed_time(e[2]) / 1e3 for e in ev]
+            for c in range(n):
+                ids = toks[c][:lim[c]]
+                if stop_at_eos:
+                    cut = next((i + 1 for i, t in enumerate(ids) if t in self.eos), len(ids))
+                    ids = ids[:cut]
+                d0 = time.perf_counter()
+                text = self.tokenizer.decode(ids, skip_special_tokens=True)
+                results.append({'text': text, 'token_ids': ids, 'ttft_s': ttft, 'ttlt_s': ttlt,
+                                'e2e_s': time.perf_counter() - start, 'mel_s': mel_s[c], 'encoder_s': enc_s[c],
+                                'decode_s': ttlt - sum(mel_s) - sum(enc_s), 'detok_s': time.perf_counter() - d0,
+                                'n_tokens': len(ids), 'batch': n})
+        return results
+
+    @torch.inference_mode()
+    def transcribe(self, audio, max_new_tokens=None, stop_at_eos=True):
+        self._check_audio(audio)
         limit = self.max_new if max_new_tokens is None else min(int(max_new_tokens), self.max_new)
         stream = torch.cuda.current_stream()
         torch.cuda.synchronize()

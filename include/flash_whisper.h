@@ -218,6 +218,41 @@ int fw_decoder_launch(const fw_decoder_t* d, int layer, int block, fw_stream_t s
 int fw_decoder_step_trace(const fw_decoder_t* d, void* trace, fw_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Batched decode step: up to FW_MAX_CLIPS independent clips per weight read (no reference
+ * counterpart: the reference decodes one clip per step, custom/model.py:107-123). Each clip's
+ * arithmetic is exactly the batch-1 step's, so its tokens equal decoding it alone with
+ * fw_decoder_step; the weights (216 MB per step without the LM head) are read once for all clips.
+ * ---------------------------------------------------------------------------------------- */
+#define FW_MAX_CLIPS 8
+
+typedef struct {
+  int n_layers, heads, max_pos, enc_len, vocab, prompt_len, clips;
+  float eps, scale;
+  const void *embed, *pos_embed, *lm_head; /* as fw_decoder_t */
+  const void *final_g, *final_b;
+  const bool *base_mask, *first_mask;
+  const int64_t* prompt;
+  fw_decoder_layer_t layers[FW_MAX_LAYERS]; /* weights as fw_decoder_t; self_k/self_v/cross_k/cross_v
+                                               point at clip 0's caches of the layer */
+  int64_t self_clip_stride;                 /* elements from clip c's self_k/self_v to clip c+1's */
+  int64_t cross_clip_stride;                /* elements from clip c's cross_k/cross_v to clip c+1's */
+  void *h, *qkv, *attn, *ffn;               /* fp16 [clips,1280], [clips,3840], [clips,1280], [clips,5120] */
+  float *part_m, *part_l, *part_acc;        /* fp32 [clips*heads*ws_splits] (m, l), [... * 64] (acc) */
+  int64_t ws_splits;                        /* >= ceil(max(max_pos, enc_len) / 64) */
+  unsigned int* counters;                   /* [clips*heads + 1], zero before the first step; left zero */
+  int64_t *cur, *state, *tokens, *best;     /* [clips], [clips,2], [clips,n_tokens], [clips] (zero) */
+  int64_t n_tokens;
+  const void *lm_q, *lm_rp;                 /* required: fw_lm_quantize output of lm_head */
+} fw_batch_decoder_t;
+
+/* Launches `steps` decode steps of every clip (fw_decoder_step semantics per clip: prompt handling,
+ * first_mask on the last prompt step, tokens appended at tokens[c * n_tokens + state[c][1]]). Per step
+ * and layer: LN1 + q/k/v, self attention with the cache write, out_proj + residual, LN2 + cross q,
+ * cross attention, cross out_proj + residual, LN3 + fc1 + GELU, fc2 + residual; then the pruned LM
+ * head of all clips with the final LN, argmax and bookkeeping (33 launches per step). */
+int fw_batch_decoder_step(const fw_batch_decoder_t* d, int steps, fw_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
  * GPU log-mel front end (custom/model.py:93-98; WhisperFeatureExtractor semantics)
  * ---------------------------------------------------------------------------------------- */
 

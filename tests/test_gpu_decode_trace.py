@@ -16,8 +16,8 @@ block, so a mismatch names the kernel:
 
 The self-attention length L = position + 1 is reached by seeding the self cache below the position
 and the state, at L in {1, 64, 224, 448} (BASELINE config 1's lengths; 448 is the last position).
-Tolerance: rtol 1e-2, atol 1e-3 on fp16 activations; bit-exact for the cache
-rows and the argmax. Weights come from varied_state_dict, whose decoder moves the argmax from step
+Tolerance: rtol 1e-2, atol 1e-3 on fp16 activations per block; bit-exact for
+the cache rows and the argmax; relative Frobenius error < 1e-2 for the oracle's own 4-layer chain. Weights come from varied_state_dict, whose decoder moves the argmax from step
 to step, with random biases and LayerNorm parameters so every bias and LN path carries signal.
 """
 
@@ -43,7 +43,8 @@ def traced_model(cuda, varied_sd):
     from flash_whisper_b200.model import CustomModel
     model = CustomModel(state_dict=varied_sd, dims=TURBO, selftest=False, capture=False)
     g = torch.Generator(device='cuda').manual_seed(7)
-    model.cross_kv.copy_((torch.randn(model.cross_kv.shape, generator=g, device='cuda') * 0.5).half())
+    with torch.inference_mode():  # the model's buffers are inference tensors
+        model.cross_kv.copy_((torch.randn(model.cross_kv.shape, generator=g, device='cuda') * 0.5).half())
     return model
 
 
@@ -67,6 +68,7 @@ def _np(t):
 
 
 @pytest.mark.parametrize('length', [1, 64, 224, 448])
+@torch.inference_mode()
 def test_fused_decode_step_activations_vs_oracle(traced_model, oracle_w, length):
     from oracle.model_np import linear, r16
     model, o, d = traced_model, oracle_w, TURBO
@@ -136,7 +138,12 @@ def test_fused_decode_step_activations_vs_oracle(traced_model, oracle_w, length)
         _, chain, _, _ = o.self_block(i, chain, pos)
         _, chain = o.cross_block(i, chain)
         chain = o.fc2(i, chain, o.fc1(i, chain))
-    _close("final residual stream vs the oracle chain", h_in, chain)
+    # End to end the two chains drift apart by fp16 rounding compounded over 4 layers (each block
+    # above is within rtol 1e-2 / atol 1e-3 of the oracle given the same input): compared by the
+    # relative Frobenius error, as the 32-layer encoder output is.
+    rel = float(np.linalg.norm(h_in - chain) / np.linalg.norm(chain))
+    assert rel < 1e-2, f'final residual stream vs the oracle chain: relative error {rel:.3e}'
+    print(f'L={length}: final residual stream vs the oracle chain, relative error {rel:.3e}')
 
     y_gpu = tr[d.decoder_layers * _lib.TRACE_LAYER:]
     y_ref, logits = o.final(h_in)

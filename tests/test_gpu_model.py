@@ -116,9 +116,31 @@ def test_tokens_bitexact_vs_reference_cuda_backend(model, turbo_sd):
     torch.cuda.empty_cache()
 
 
-def test_varied_tokens_bitexact_vs_reference_cuda_backend(cuda):
-    """224 greedy tokens on weights whose output changes every few steps, identical to the
-    reference's CUDA backend (its own kernels + cuBLAS projections) on the same weights and audio."""
+def _logits_at(m, audio, step):
+    """fp16 logits [vocab] (as float32) of decode step `step` (the step that emits token `step`) of
+    m's own greedy run on `audio`, from the final LayerNorm row fw_decoder_step_trace records."""
+    from flash_whisper_b200 import _lib
+    m.load_audio(audio)
+    m.run_front()
+    m.run_prompt()
+    if step == 0:
+        raise ValueError('step 0 is emitted by the prompt')
+    m.run_steps(step - 1)
+    trace = torch.zeros(m.dims.decoder_layers * _lib.TRACE_LAYER + m.dims.d_model, dtype=torch.float16,
+                        device='cuda')
+    m.ext.decoder_step_trace(m.dec_desc, trace)
+    y = trace[-m.dims.d_model:].float()
+    return (m.dec.lm_head.float() @ y).half().float()
+
+
+@torch.inference_mode()
+def test_varied_tokens_vs_reference_cuda_backend(cuda):
+    """224 greedy tokens on weights whose output changes every few steps, against the reference's
+    CUDA backend (its own kernels around cuBLAS projections) on the same weights and audio. The
+    LayerNorm, attention and LM-head arithmetic are the reference kernels' own, so the two runs are
+    identical until the first step where the reference's cuBLAS projection sums and this package's
+    fused ones round an fp16 logit differently. Such a divergence must be an fp16 near-tie: the
+    two candidates' logits in this package's own step within two fp16 ulps of each other."""
     from oracle.build_ref import load_ref
     if load_ref() is None:
         pytest.skip('oracle/_ref not built')
@@ -133,10 +155,19 @@ def test_varied_tokens_bitexact_vs_reference_cuda_backend(cuda):
     torch.cuda.empty_cache()
     m = CustomModel(state_dict=sd, dims=TURBO, selftest=False)
     got = m.transcribe(audio, max_new_tokens=224, stop_at_eos=False)['token_ids']
-    first_diff = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
-    print('varied weights: distinct tokens', len(set(want)), 'first divergence', first_diff)
+    k = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
+    print('varied weights: distinct tokens', len(set(want)), 'first divergence', k)
     assert len(set(want)) > 20
-    assert got == want, f'first divergence at step {first_diff}'
+    if k is not None:
+        logits = _logits_at(m, audio, k)
+        top = float(logits.max())
+        ulp = 2.0 ** (np.floor(np.log2(abs(top))) - 10)
+        assert top - float(logits[got[k]]) <= ulp  # the fp32 matmul here may round one ulp apart
+        gap = top - float(logits[want[k]])
+        print(f'step {k}: ours {got[k]} ({top:.5f}), reference {want[k]} ({float(logits[want[k]]):.5f}), '
+              f'gap {gap:.2e} = {gap / ulp:.1f} fp16 ulps')
+        assert gap <= 2 * ulp, f'divergence at step {k} is not an fp16 near-tie (gap {gap / ulp:.1f} ulps)'
+        assert k >= 32
     del m
     torch.cuda.empty_cache()
 
