@@ -103,6 +103,10 @@ _SIGNATURES = {
     'fw_decoder_step_trace': (c_int, [POINTER(Decoder), vp, vp]),
     'fw_decoder_launch': (c_int, [POINTER(Decoder), c_int, c_int, vp]),
     'fw_batch_decoder_step': (c_int, [POINTER(BatchDecoder), c_int, vp]),
+    'fw_batch_decoder_launch': (c_int, [POINTER(BatchDecoder), c_int, c_int, vp]),
+    'fw_decode_loop_create': (c_int, [POINTER(Decoder), vp, c_int, POINTER(vp)]),
+    'fw_decode_loop_launch': (c_int, [vp, vp]),
+    'fw_decode_loop_destroy': (c_int, [vp]),
     'fw_log_mel': (c_int, [vp, c_int, c_int, vp, vp, vp, vp, c_int, vp]),
     'fw_gemm_f16': (c_int, [vp, c_int64, vp, c_int64, vp, vp, c_int64, vp, c_int64, c_int, c_int, c_int, c_int,
                             c_float, c_int, vp]),

@@ -139,6 +139,20 @@ class BatchDecoder:
         if count % self.chunk:
             self.model.ext.batch_decoder_step(self._desc(n), count % self.chunk)
 
+    def prepare(self, n):
+        """Captures, before any use, the encoder graphs of slots 0..n-1 and the chunk graph of n clips
+        (the warm-up launches they need change this decoder's state)."""
+        m = self.model
+        for slot in range(n):
+            if self.enc_graphs[slot] is None:
+                m.ext.encoder_forward(self.enc_descs[slot])
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    m.ext.encoder_forward(self.enc_descs[slot])
+                self.enc_graphs[slot] = g
+        self._chunk_graph(n)
+        torch.cuda.synchronize()
+
     def decode(self, n, n_tokens):
         """Prompt + n_tokens - 1 steps of the first n clips, whose cross caches are already filled.
         Clip c's tokens are then self.tokens[c, :n_tokens]."""
@@ -146,3 +160,81 @@ class BatchDecoder:
             self._chunk_graph(n)
         self.prompt(n)
         self.steps(n, max(0, n_tokens - 1))
+
+
+class HostStaging:
+    """Pinned host buffers for clips copied in asynchronously: buffer k is rewritten only after the
+    copy that last read it has completed."""
+
+    def __init__(self, count, n_samples):
+        self.bufs = [torch.zeros(n_samples, dtype=torch.float32).pin_memory() for _ in range(count)]
+        self.events = [None] * count
+        self.next = 0
+
+    def copy_in(self, audio, dst, stream):
+        k = self.next
+        self.next = (k + 1) % len(self.bufs)
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        buf = self.bufs[k].numpy()
+        buf[:audio.size] = audio
+        buf[audio.size:] = 0.0
+        dst.copy_(self.bufs[k], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.events[k] = ev
+
+
+@torch.inference_mode()
+def run_clips(model, decoders, waves, n_tokens, host_audio=None, staging=None):
+    """Decodes many clips through two batched decoders on two CUDA streams.
+
+    Clips are taken in order, `decoders[0].clips` at a time (group g uses decoders[g % 2]). On the
+    front-end stream the log-mel and encoder of every clip of group g+1 run while the decode stream
+    decodes group g, so the tensor-core encoder overlaps the memory-bound decode. waves: device
+    float32 [n, 480000], or None with host_audio (float32 numpy clips, copied in on the front-end
+    stream through `staging`, a HostStaging). Returns the token tensor [n, max_pos] on the host (clip
+    i's tokens in its first n_tokens[i] entries) and per-clip (log-mel, encoder) device times in s.
+    """
+    clips = decoders[0].clips
+    n_all = len(n_tokens)
+    groups = [list(range(g, min(g + clips, n_all))) for g in range(0, n_all, clips)]
+    for bd in decoders:
+        bd.prepare(clips)
+    for g, grp in enumerate(groups):
+        if len(grp) != clips:
+            decoders[g % 2].prepare(len(grp))
+    cur = torch.cuda.current_stream()
+    front, back = torch.cuda.Stream(), torch.cuda.Stream()
+    front.wait_stream(cur)
+    back.wait_stream(cur)
+    tokens = torch.zeros(n_all, model.max_pos, dtype=torch.long).pin_memory()
+    enc_done = [torch.cuda.Event() for _ in groups]
+    dec_done = [torch.cuda.Event() for _ in groups]
+    stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_all)]
+    for g, grp in enumerate(groups):
+        bd = decoders[g % 2]
+        with torch.cuda.stream(front):
+            if g >= 2:
+                front.wait_event(dec_done[g - 2])  # the slot set of group g - 2 is free again
+            for c, i in enumerate(grp):
+                stage_ev[i][0].record(front)
+                if waves is not None:
+                    model.wave.copy_(waves[i])
+                else:
+                    staging.copy_in(host_audio[i], model.wave, front)
+                model.run_mel()
+                stage_ev[i][1].record(front)
+                bd.encoder_slot(c)
+                stage_ev[i][2].record(front)
+            enc_done[g].record(front)
+        with torch.cuda.stream(back):
+            back.wait_event(enc_done[g])
+            bd.decode(len(grp), max(n_tokens[i] for i in grp))
+            tokens[grp[0]:grp[-1] + 1].copy_(bd.tokens[:len(grp)], non_blocking=True)
+            dec_done[g].record(back)
+    cur.wait_stream(front)
+    cur.wait_stream(back)
+    torch.cuda.synchronize()
+    times = [(e[0].elapsed_time(e[1]) / 1e3, e[1].elapsed_time(e[2]) / 1e3) for e in stage_ev]
+    return tokens, times

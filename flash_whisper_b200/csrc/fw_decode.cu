@@ -81,6 +81,50 @@ __device__ __forceinline__ float ln_apply(float v, float mean, float inv, float 
   return fmaf((v - mean) * inv, g, b);
 }
 
+// ln1280_stats of the first C of kClips rows at once (two barriers for all of them): every row's
+// statistics are formed in exactly ln1280_stats' order. red: kClips x 16 floats of shared memory.
+template <int kClips>
+__device__ __forceinline__ void ln1280_stats_clips(const float (&v)[kClips][5], float (*red)[16], int C, float eps,
+                                                   float (&mean)[kClips], float (&inv)[kClips]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int c = 0; c < kClips; ++c) {
+    if (c >= C) break;
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) sum += v[c][i];
+    sum = warp_sum(sum);
+    if (lane == 0) red[c][warp] = sum;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < kClips; ++c) {
+    if (c >= C) break;
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m += red[c][i];
+    m /= static_cast<float>(kHidden);
+    mean[c] = m;
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const float d = v[c][i] - m;
+      sq = fmaf(d, d, sq);
+    }
+    sq = warp_sum(sq);
+    if (lane == 0) red[c][8 + warp] = sq;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < kClips; ++c) {
+    if (c >= C) break;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) var += red[c][8 + i];
+    inv[c] = rsqrtf(var / static_cast<float>(kHidden) + eps);
+  }
+}
+
 // Dot product of one 1280-wide fp16 row (16-byte chunks lane + 32*c) with x held as 40 floats per
 // lane in the same chunk order. The fma order is the reference LM-head order (whisper_kernels.cu:58-68).
 __device__ __forceinline__ float dot1280_lane(const uint4* row, const float (&xf)[40]) {
@@ -1160,6 +1204,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ float red[16];
+  __shared__ float red_clips[kClips][16];
   __shared__ __align__(16) float4 rps[kLmMaxRowsPerCta];
   __shared__ uint8_t msk[2][kLmMaxRowsPerCta];
   __shared__ float warp_l[kClips][8], warp_b[kClips][8], xstat[kClips][2][8];
@@ -1236,12 +1281,36 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   // LayerNorm of each clip's row (ln1280_stats order; consecutive calls may share `red`), its
   // max|x| and |x|_1, and the B operand rows 2c (x_hi) and 2c + 1 (x_lo) of xq = rint(x / sx).
   float xv[kClips][5];
+  if constexpr (kClips > 1) {
+    if (kLN) {
+      float mean[kClips], inv[kClips];
+#pragma unroll
+      for (int c = 0; c < kClips; ++c) {
+        if (c >= C) break;
+#pragma unroll
+        for (int i = 0; i < 5; ++i) xv[c][i] = __half2float(p.h[c * kHidden + threadIdx.x + i * 256]);
+      }
+      ln1280_stats_clips<kClips>(xv, red_clips, C, p.eps, mean, inv);
+#pragma unroll
+      for (int c = 0; c < kClips; ++c) {
+        if (c >= C) break;
+#pragma unroll
+        for (int i = 0; i < 5; ++i) {
+          const half y = __float2half(ln_apply(xv[c][i], mean[c], inv[c], g[i], be[i]));
+          ys[c * kHidden + threadIdx.x + i * 256] = y;
+          xv[c][i] = __half2float(y);
+        }
+      }
+    }
+  }
 #pragma unroll
   for (int c = 0; c < kClips; ++c) {
     if (c >= C) break;
     const half* hc = p.h + c * kHidden;
     half* yc = ys + c * kHidden;
-    if (kLN) {
+    if (kLN && kClips > 1) {
+      // normalised above
+    } else if (kLN) {
 #pragma unroll
       for (int i = 0; i < 5; ++i) xv[c][i] = __half2float(hc[threadIdx.x + i * 256]);
       float mean, inv;
@@ -1394,31 +1463,40 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       const int li = t * kQTileRows + q * 32 + lane;
-      if (li < nrows) {
-        const float4 prm = rps[li];
-        bool fetch = false;
+      const bool row_ok = li < nrows;
+      const float4 prm = row_ok ? rps[li] : make_float4(0.f, 0.f, 0.f, 0.f);
+      bool fetch = false;
 #pragma unroll
-        for (int c = 0; c < kClips; ++c) {
-          if (c >= C) break;
-          const int sum = 128 * static_cast<int>(vv[2 * c]) + static_cast<int>(vv[2 * c + 1]);  // exact
-          const float approx = prm.x * sx[c] * static_cast<float>(sum);
-          const float b = (nx1[c] * prm.y + sx[c] * prm.z + 4e-7f * fabsf(approx)) * 1.00001f + 1e-30f;
-          if (maskc[c][li]) {
-            ub[c * kLmMaxRowsPerCta + li] = -INFINITY;
-          } else {
-            ub[c * kLmMaxRowsPerCta + li] = approx + b;
-            lmax[c] = fmaxf(lmax[c], approx - b);
-            bmax[c] = fmaxf(bmax[c], b);
-            if (!isfinite(approx) || !isfinite(b)) bmax[c] = INFINITY;
-            // Rows that may survive the selection (against the lower bounds seen so far) have their
-            // fp16 row fetched into L2 now, so the exact pass reads them from L2. A hint only.
-            const float lo = approx - b;
-            const float run = fmaxf(ordered_to_float(atomicMax(&s_lo_max[c], float_to_ordered(lo))), lo);
-            if (approx + b >= run - (0x1p-9f * (fabsf(run) + 2.f * b) + 0x1p-23f)) fetch = true;
-          }
+      for (int c = 0; c < kClips; ++c) {
+        if (c >= C) break;
+        const int sum = 128 * static_cast<int>(vv[2 * c]) + static_cast<int>(vv[2 * c + 1]);  // exact
+        const float approx = prm.x * sx[c] * static_cast<float>(sum);
+        const float b = (nx1[c] * prm.y + sx[c] * prm.z + 4e-7f * fabsf(approx)) * 1.00001f + 1e-30f;
+        const bool live = row_ok && !maskc[c][li];
+        if (row_ok) ub[c * kLmMaxRowsPerCta + li] = live ? approx + b : -INFINITY;
+        const float lo = live ? approx - b : -INFINITY;
+        if (live) {
+          lmax[c] = fmaxf(lmax[c], lo);
+          bmax[c] = fmaxf(bmax[c], b);
+          if (!isfinite(approx) || !isfinite(b)) bmax[c] = INFINITY;
         }
-        if (fetch) l2_prefetch(p.w + static_cast<size_t>(r0 + li) * kHidden, kHidden * 2);
+        // Rows that may survive the selection (against the lower bounds seen so far) have their fp16
+        // row fetched into L2 now, so the exact pass reads them from L2. A hint only. With several
+        // clips the running maximum is updated once per warp (the lanes' own maximum first) so that
+        // 32 lanes do not serialise on the same shared-memory word.
+        float run;
+        if constexpr (kClips == 1) {
+          run = live ? fmaxf(ordered_to_float(atomicMax(&s_lo_max[c], float_to_ordered(lo))), lo) : lo;
+        } else {
+          const float wlo = warp_max(lo);
+          unsigned prev = 0;
+          if (lane == 0) prev = atomicMax(&s_lo_max[c], float_to_ordered(wlo));
+          prev = __shfl_sync(0xffffffffu, prev, 0);
+          run = fmaxf(ordered_to_float(prev), wlo);
+        }
+        if (live && approx + b >= run - (0x1p-9f * (fabsf(run) + 2.f * b) + 0x1p-23f)) fetch = true;
       }
+      if (fetch) l2_prefetch(p.w + static_cast<size_t>(r0 + li) * kHidden, kHidden * 2);
     }
   }
 #pragma unroll
@@ -1454,15 +1532,22 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   }
   __syncthreads();
 
-  // ---- pass 2: exact fp16 logits of the surviving rows, four rows per warp at a time ----
+  // ---- pass 2: exact fp16 logits of the surviving rows, four rows per warp at a time; with several
+  // clips, warp w rescores clip w's survivors (the 8 warps work on the 8 clips in parallel) ----
+  static_assert(kClips == 1 || kClips == 8, "pass 2 maps warp w to clip w");
+  if (kClips > 1 && lane == 0) {
+#pragma unroll
+    for (int c = 0; c < kClips; ++c) warp_best[c][warp] = 0ull;  // this warp's entry of every clip
+  }
 #pragma unroll 1
-  for (int c = 0; c < C; ++c) {
+  for (int c = (kClips == 1 ? 0 : warp); c < (kClips == 1 ? C : min(C, warp + 1)); ++c) {
     float xf[40];
     load_x40(ys + c * kHidden, xf);
     const int nc = ncand[c];
     const unsigned short* cl = cand + c * kLmMaxRowsPerCta;
     unsigned long long mine = 0;
-    for (int j = 4 * warp; j < nc; j += 32) {
+    const int j0 = kClips == 1 ? 4 * warp : 0, jstep = kClips == 1 ? 32 : 4;
+    for (int j = j0; j < nc; j += jstep) {
       int rr[4];
       const half* rows[4];
 #pragma unroll
@@ -1876,22 +1961,36 @@ struct BatchGemvParams {
 };
 
 // LayerNorm (+ optional GELU epilogue) GEMV for every clip: out_c[r] = act(W[r] . LN(h_c) + b[r]).
-// The CTA's 8 * kRowsPerWarp weight rows are bulk-copied into shared memory before the PDL wait;
-// the LayerNorm rows of all clips are kept in shared memory as fp32 (exact fp16 values). Warp w
-// owns rows w, w + 8, ...: per 16-byte weight chunk it loads the chunk of each of its rows once and
-// runs every clip's fma chain (the lane order of dot1280_lane) from one read of that clip's x chunk.
+// 512 threads: the two halves of the CTA handle clips 0-3 and 4-7. Each half computes its clips'
+// LayerNorm exactly as a 256-thread add_layernorm_kernel does (ln1280_stats order) and stores the
+// normalised rows as fp32 (exact fp16 values) in two planes per clip, elements 0-3 and 4-7 of every
+// 8-element chunk, so a lane's float4 reads of its chunk are consecutive across the warp. The CTA's
+// 8 * kRowsPerWarp weight rows are bulk-copied into shared memory before the PDL wait. Warp w of a
+// half owns rows w, w + 8, ...: per 16-byte chunk it converts each of its rows' chunk to fp32 once and
+// runs the fma chains of its four clips (the lane order of dot1280_lane), then the warp xor-tree.
+constexpr int kBlnThreads = 512;
+
+template <int kRowsPerWarp>
+struct BlnShape {
+  static constexpr int kRows = 8 * kRowsPerWarp;
+  static constexpr int kWBytes = kRows * kHidden * 2;
+  static constexpr int kSmem = kWBytes + kMaxClips * kHidden * 4;
+};
+
 template <int kAct, int kRowsPerWarp, bool kEmbed>
-__global__ void __launch_bounds__(256) bln_gemv_kernel(BatchGemvParams p) {
+__global__ void __launch_bounds__(kBlnThreads, 1) bln_gemv_kernel(BatchGemvParams p) {
+  using S = BlnShape<kRowsPerWarp>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ float red[kMaxClips][16];
-  constexpr int kRows = 8 * kRowsPerWarp;
   half* ws = reinterpret_cast<half*>(smem);
-  float* xs = reinterpret_cast<float*>(smem + kRows * kHidden * 2);
+  float4* xs = reinterpret_cast<float4*>(smem + S::kWBytes);  // clip c: plane A [160], plane B [160]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int r0 = blockIdx.x * kRows;
-  const int nr = min(kRows, p.n_out - r0);
+  const int half_id = warp >> 3, wr = warp & 7, t256 = tid & 255;
+  const int r0 = blockIdx.x * S::kRows;
+  const int nr = min(S::kRows, p.n_out - r0);
   const int C = p.clips;
+  const int c0 = 4 * half_id;  // this half's clips c0 .. c0 + 3
   if (tid == 0) {
     mbar_init(&bar, 1);
     mbar_fence_init();
@@ -1905,119 +2004,130 @@ __global__ void __launch_bounds__(256) bln_gemv_kernel(BatchGemvParams p) {
   float g[5], be[5], bias[kRowsPerWarp];
 #pragma unroll
   for (int i = 0; i < 5; ++i) {
-    g[i] = __half2float(p.gamma[tid + i * 256]);
-    be[i] = __half2float(p.beta[tid + i * 256]);
+    g[i] = __half2float(p.gamma[t256 + i * 256]);
+    be[i] = __half2float(p.beta[t256 + i * 256]);
   }
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int r = warp + 8 * i;
+    const int r = wr + 8 * i;
     bias[i] = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
   }
   __syncthreads();
   pdl_wait();
   pdl_trigger();
 
-  // LayerNorm of every clip (ln1280_stats order: per-thread sums, warp xor-tree, warps in order)
-  float v[kMaxClips][5];
+  // LayerNorm of this half's clips, thread t256 holding elements t256 + 256 i as in ln1280_stats
+  float v[4][5];
 #pragma unroll
-  for (int c = 0; c < kMaxClips; ++c) {
+  for (int cc = 0; cc < 4; ++cc) {
+    const int c = c0 + cc;
     if (c >= C) break;
     if (kEmbed) {
       const int64_t raw = p.state[2 * c];
       const int pos = static_cast<int>(min(max(raw, int64_t(0)), int64_t(p.max_pos - 1)));
       int64_t tok = pos < p.prompt_len ? p.prompt[pos] : p.cur[c];
       if (raw < 0 || raw >= p.max_pos || tok < 0 || tok >= p.vocab) {
-        if (tid == 0 && blockIdx.x == 0) flag_error(FW_DEVERR_BAD_INDEX);
+        if (t256 == 0 && blockIdx.x == 0) flag_error(FW_DEVERR_BAD_INDEX);
         tok = tok < 0 ? 0 : (tok >= p.vocab ? p.vocab - 1 : tok);
       }
       const half* er = p.embed + static_cast<size_t>(tok) * kHidden;
       const half* pr = p.pos_embed + static_cast<size_t>(pos) * kHidden;
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
-        v[c][i] = round_half(__half2float(er[tid + i * 256]) + __half2float(pr[tid + i * 256]));
-        if (blockIdx.x == 0) p.h_out[c * kHidden + tid + i * 256] = __float2half(v[c][i]);
+        v[cc][i] = round_half(__half2float(er[t256 + i * 256]) + __half2float(pr[t256 + i * 256]));
+        if (blockIdx.x == 0) p.h_out[c * kHidden + t256 + i * 256] = __float2half(v[cc][i]);
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 5; ++i) v[c][i] = __half2float(p.h[c * kHidden + tid + i * 256]);
+      for (int i = 0; i < 5; ++i) v[cc][i] = __half2float(p.h[c * kHidden + t256 + i * 256]);
     }
     float sum = 0.f;
 #pragma unroll
-    for (int i = 0; i < 5; ++i) sum += v[c][i];
+    for (int i = 0; i < 5; ++i) sum += v[cc][i];
     sum = warp_sum(sum);
-    if (lane == 0) red[c][warp] = sum;
+    if (lane == 0) red[c][wr] = sum;
   }
   __syncthreads();
-  float mean[kMaxClips];
+  float mean[4];
 #pragma unroll
-  for (int c = 0; c < kMaxClips; ++c) {
+  for (int cc = 0; cc < 4; ++cc) {
+    const int c = c0 + cc;
     if (c >= C) break;
     float m = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) m += red[c][i];
     m /= static_cast<float>(kHidden);
-    mean[c] = m;
+    mean[cc] = m;
     float sq = 0.f;
 #pragma unroll
     for (int i = 0; i < 5; ++i) {
-      const float d = v[c][i] - m;
+      const float d = v[cc][i] - m;
       sq = fmaf(d, d, sq);
     }
     sq = warp_sum(sq);
-    if (lane == 0) red[c][8 + warp] = sq;
+    if (lane == 0) red[c][8 + wr] = sq;
   }
   __syncthreads();
 #pragma unroll
-  for (int c = 0; c < kMaxClips; ++c) {
+  for (int cc = 0; cc < 4; ++cc) {
+    const int c = c0 + cc;
     if (c >= C) break;
     float var = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) var += red[c][8 + i];
     const float inv = rsqrtf(var / static_cast<float>(kHidden) + p.eps);
+    float* plane = reinterpret_cast<float*>(xs + c * 2 * (kHidden / 8));
 #pragma unroll
-    for (int i = 0; i < 5; ++i)
-      xs[c * kHidden + tid + i * 256] = __half2float(__float2half(ln_apply(v[c][i], mean[c], inv, g[i], be[i])));
+    for (int i = 0; i < 5; ++i) {
+      const int k = t256 + i * 256, q = k >> 3, e = k & 7;
+      const float y = __half2float(__float2half(ln_apply(v[cc][i], mean[cc], inv, g[i], be[i])));
+      plane[(e < 4 ? q : (kHidden / 8) + q) * 4 + (e & 3)] = y;
+    }
   }
   __syncthreads();
   if (nr > 0 && !mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
 
-  float acc[kRowsPerWarp][kMaxClips];
+  float acc[kRowsPerWarp][4];
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
-    for (int c = 0; c < kMaxClips; ++c) acc[i][c] = 0.f;
+    for (int cc = 0; cc < 4; ++cc) acc[i][cc] = 0.f;
 #pragma unroll
   for (int ch = 0; ch < 5; ++ch) {
-    uint4 wv[kRowsPerWarp];
+    float wf[kRowsPerWarp][8];
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i)
-      wv[i] = reinterpret_cast<const uint4*>(ws + (warp + 8 * i) * kHidden)[lane + 32 * ch];
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const uint4 wv = reinterpret_cast<const uint4*>(ws + (wr + 8 * i) * kHidden)[lane + 32 * ch];
+      const half2* h2 = reinterpret_cast<const half2*>(&wv);
 #pragma unroll
-    for (int c = 0; c < kMaxClips; ++c) {
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(h2[k]);
+        wf[i][2 * k] = f.x;
+        wf[i][2 * k + 1] = f.y;
+      }
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const int c = c0 + cc;
       if (c >= C) break;
-      const float4* xp = reinterpret_cast<const float4*>(xs + c * kHidden + (lane + 32 * ch) * 8);
-      const float4 xa = xp[0], xb = xp[1];
+      const float4 xa = xs[c * 2 * (kHidden / 8) + lane + 32 * ch];
+      const float4 xb = xs[c * 2 * (kHidden / 8) + (kHidden / 8) + lane + 32 * ch];
       const float x8[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i) {
-        const half2* h2 = reinterpret_cast<const half2*>(&wv[i]);
+      for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = __half22float2(h2[k]);
-          acc[i][c] = fmaf(f.x, x8[2 * k], acc[i][c]);
-          acc[i][c] = fmaf(f.y, x8[2 * k + 1], acc[i][c]);
-        }
-      }
+        for (int e = 0; e < 8; ++e) acc[i][cc] = fmaf(wf[i][e], x8[e], acc[i][cc]);
     }
   }
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int r = warp + 8 * i;
+    const int r = wr + 8 * i;
 #pragma unroll
-    for (int c = 0; c < kMaxClips; ++c) {
+    for (int cc = 0; cc < 4; ++cc) {
+      const int c = c0 + cc;
       if (c >= C) break;
-      const float a = warp_sum(acc[i][c]);
-      if (lane == c && r < nr) {
+      const float a = warp_sum(acc[i][cc]);
+      if (lane == cc && r < nr) {
         float o = round_half(a + bias[i]);
         if (kAct == 1) o = gelu_erf(o);
         p.out[static_cast<size_t>(c) * p.out_stride + r0 + r] = __float2half(o);
@@ -2029,12 +2139,17 @@ __global__ void __launch_bounds__(256) bln_gemv_kernel(BatchGemvParams p) {
 // Output projection of the attention heads + bias + residual for every clip:
 // h_c[r] = fp16(h_c[r] + fp16(sum_head (W_o[head][r] . o_c[head]) + b[r])) with W_o head-major
 // [heads, 1280, 64]. Per (row, head) the dot is the two-chain rotated-chunk order of
-// head_block_kernel's output-projection partial and the head sum runs in head order, so the result
-// equals head_block_kernel's. The CTA's kOutRowsB rows of every head are bulk-copied into shared
-// memory before the PDL wait. Thread (row, clip, group) computes the partials of kHeadsPerGroup heads.
-constexpr int kOutRowsB = 10;      // 1280 / 10 = 128 CTAs
-constexpr int kHeadsPerGroup = 5;  // 20 heads = 4 groups
-constexpr int kOutThreadsB = kOutRowsB * kMaxClips * (kHeads / kHeadsPerGroup);  // 320
+// head_block_kernel's output-projection partial (chunk (j + r) mod 8 at step j, even and odd steps in
+// separate chains), and the head sum runs in head order, so the result equals head_block_kernel's.
+// A CTA owns kOutRowsB = 16 rows; its slice of every head (16 x 64 fp16) is bulk-copied into shared
+// memory before the PDL wait. Thread (k, clip pair, head pair) computes rows r0 + k and r0 + k + 8 (the
+// same rotation, so each o chunk read serves both rows) for two clips and two heads; the attention
+// outputs are staged as fp32 in two planes (elements 0-3 and 4-7 of every chunk) so a warp's float4
+// reads are conflict-free. The per-head partials meet in shared memory and are summed in head order.
+constexpr int kOutRowsB = 16;                                   // 1280 / 16 = 80 CTAs
+constexpr int kOutThreadsB = 320;                               // 8 row pairs x 4 clip pairs x 10 head pairs
+constexpr int kBoutWBytes = kHeads * kOutRowsB * kHeadDim * 2;  // 40 KB
+constexpr int kBoutSmem = kBoutWBytes + kMaxClips * kHidden * 4 + kOutRowsB * kMaxClips * kHeads * 4;
 
 struct BatchOutParams {
   const half* wo;    // head-major [heads, 1280, 64]
@@ -2044,77 +2159,121 @@ struct BatchOutParams {
   int clips;
 };
 
-constexpr int kBoutSmem = kHeads * kOutRowsB * kHeadDim * 2 + kMaxClips * kHidden * 4;  // 25.6 KB + 40 KB
-
-__global__ void __launch_bounds__(kOutThreadsB) bout_residual_kernel(BatchOutParams p) {
+__global__ void __launch_bounds__(kOutThreadsB, 1) bout_residual_kernel(BatchOutParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  auto ws = reinterpret_cast<half (*)[kOutRowsB][kHeadDim]>(smem);                           // [heads][rows][64]
-  auto os = reinterpret_cast<float (*)[kHidden]>(smem + kHeads * kOutRowsB * kHeadDim * 2);  // [clips][1280]
-  __shared__ float part[kOutRowsB][kMaxClips][kHeads];
+  const half* ws = reinterpret_cast<const half*>(smem);                    // [heads][16 rows][64]
+  float4* os = reinterpret_cast<float4*>(smem + kBoutWBytes);             // clip c: A [160], B [160]
+  float* part = reinterpret_cast<float*>(smem + kBoutWBytes + kMaxClips * kHidden * 4);  // [16][8][20]
   __shared__ __align__(8) uint64_t bar;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = blockIdx.x * kOutRowsB;
   const int C = p.clips;
   if (tid == 0) {
     mbar_init(&bar, 1);
     mbar_fence_init();
-    mbar_arrive_expect_tx(&bar, kHeads * kOutRowsB * kHeadDim * 2);
+    mbar_arrive_expect_tx(&bar, kBoutWBytes);
     const uint64_t pol = policy_evict_first();
     for (int hh = 0; hh < kHeads; ++hh)
-      bulk_g2s_stream(&ws[hh][0][0], p.wo + (static_cast<size_t>(hh) * kHidden + r0) * kHeadDim,
+      bulk_g2s_stream(smem + hh * kOutRowsB * kHeadDim * 2, p.wo + (static_cast<size_t>(hh) * kHidden + r0) * kHeadDim,
                       kOutRowsB * kHeadDim * 2, &bar, pol);
   }
-  const int rl = tid % kOutRowsB, c = (tid / kOutRowsB) % kMaxClips, grp = tid / (kOutRowsB * kMaxClips);
-  const int r = r0 + rl;
-  const float obias = p.bo ? __half2float(p.bo[r]) : 0.f;
+  // epilogue owner: (row, clip) = (tid % 16, tid / 16) for tid < 128
+  const bool owner = tid < kOutRowsB * kMaxClips && tid / kOutRowsB < C;
+  const float obias = (p.bo && owner) ? __half2float(p.bo[r0 + tid % kOutRowsB]) : 0.f;
   __syncthreads();
   pdl_wait();
   pdl_trigger();
-  for (int i = tid; i < C * kHidden; i += kOutThreadsB) os[i / kHidden][i % kHidden] = __half2float(p.attn[i]);
+  for (int i = tid; i < C * kHidden; i += kOutThreadsB) {
+    const int c = i / kHidden, k = i % kHidden, q = k >> 3, e = k & 7;
+    reinterpret_cast<float*>(os + c * 2 * (kHidden / 8))[(e < 4 ? q : (kHidden / 8) + q) * 4 + (e & 3)] =
+        __half2float(p.attn[i]);
+  }
   __syncthreads();
   if (!mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
-  if (c < C) {
+  const int k = lane & 7, cp = lane >> 3, hp = warp;  // rows r0+k, r0+k+8; clips 2cp, 2cp+1; heads 2hp, 2hp+1
+  const int c0 = 2 * cp;
+  if (c0 < C) {
+    const bool two = c0 + 1 < C;
 #pragma unroll
-    for (int q = 0; q < kHeadsPerGroup; ++q) {
-      const int hh = grp * kHeadsPerGroup + q;
-      const uint4* wr = reinterpret_cast<const uint4*>(&ws[hh][rl][0]);
-      const float4* o4 = reinterpret_cast<const float4*>(&os[c][hh * kHeadDim]);
-      float acc2[2] = {0.f, 0.f};
+    for (int q = 0; q < 2; ++q) {
+      const int hh = 2 * hp + q;
+      const uint4* wa = reinterpret_cast<const uint4*>(ws + (hh * kOutRowsB + k) * kHeadDim);
+      const uint4* wb = reinterpret_cast<const uint4*>(ws + (hh * kOutRowsB + k + 8) * kHeadDim);
+      float acc[2][2][2] = {};  // [row][clip][chain]
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int ch = (j + r) & 7;  // head_block_kernel's rotation (its row index mod 8 equals r's)
-        const uint4 wv = wr[ch];
-        const float4 oa = o4[2 * ch], ob = o4[2 * ch + 1];
-        const half2* w2 = reinterpret_cast<const half2*>(&wv);
-        const float2 f0 = __half22float2(w2[0]), f1 = __half22float2(w2[1]);
-        const float2 f2 = __half22float2(w2[2]), f3 = __half22float2(w2[3]);
-        float& a = acc2[j & 1];
-        a = fmaf(f0.x, oa.x, a);
-        a = fmaf(f0.y, oa.y, a);
-        a = fmaf(f1.x, oa.z, a);
-        a = fmaf(f1.y, oa.w, a);
-        a = fmaf(f2.x, ob.x, a);
-        a = fmaf(f2.y, ob.y, a);
-        a = fmaf(f3.x, ob.z, a);
-        a = fmaf(f3.y, ob.w, a);
+        const int ch = (j + r0 + k) & 7;  // head_block_kernel's rotation (its row index mod 8 equals r's)
+        float w8[2][8];
+        const uint4 wva = wa[ch], wvb = wb[ch];
+        const half2* a2 = reinterpret_cast<const half2*>(&wva);
+        const half2* b2 = reinterpret_cast<const half2*>(&wvb);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fa = __half22float2(a2[e]), fb = __half22float2(b2[e]);
+          w8[0][2 * e] = fa.x;
+          w8[0][2 * e + 1] = fa.y;
+          w8[1][2 * e] = fb.x;
+          w8[1][2 * e + 1] = fb.y;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          if (cc == 1 && !two) break;
+          const int c = c0 + cc;
+          const float4 oa = os[c * 2 * (kHidden / 8) + hh * 8 + ch];
+          const float4 ob = os[c * 2 * (kHidden / 8) + (kHidden / 8) + hh * 8 + ch];
+          const float o8[8] = {oa.x, oa.y, oa.z, oa.w, ob.x, ob.y, ob.z, ob.w};
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            float& a = acc[rr][cc][j & 1];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a = fmaf(w8[rr][e], o8[e], a);
+          }
+        }
       }
-      part[rl][c][hh] = acc2[0] + acc2[1];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+          if (cc == 0 || two) part[((k + 8 * rr) * kMaxClips + c0 + cc) * kHeads + hh] = acc[rr][cc][0] + acc[rr][cc][1];
     }
   }
   __syncthreads();
-  if (grp == 0 && c < C) {
+  if (owner) {
+    const int rl = tid % kOutRowsB, c = tid / kOutRowsB;
     float acc = 0.f;
 #pragma unroll
-    for (int hh = 0; hh < kHeads; ++hh) acc += part[rl][c][hh];
-    half* hr = p.h + static_cast<size_t>(c) * kHidden + r;
+    for (int hh = 0; hh < kHeads; ++hh) acc += part[(rl * kMaxClips + c) * kHeads + hh];
+    half* hr = p.h + static_cast<size_t>(c) * kHidden + r0 + rl;
     *hr = __float2half(__half2float(*hr) + round_half(acc + obias));
   }
 }
 
+// Sum of 32 per-lane values v[0..31] over the 32 lanes of a warp, returning in lane l the sum of
+// index l: the xor butterfly of warp_sum (distances 16, 8, 4, 2, 1) applied to all 32 values at once,
+// each level halving the values a lane keeps (it adds the partner's copy of the half it keeps and
+// hands over the other half). Every sum is formed from the same operands in the same tree as
+// warp_sum(v[l]), so the result is bit-identical to it; 31 shuffles instead of 160.
+__device__ __forceinline__ float warp_sum32_transpose(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int d = 16, n = 16; d > 0; d >>= 1, n >>= 1) {
+    const bool up = (lane & d) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float send = up ? v[i] : v[n + i];
+      const float keep = up ? v[n + i] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+    }
+  }
+  return v[0];
+}
+
 // fc2 + residual for every clip: h_c[r] = fp16(h_c[r] + fp16(W[r] . x_c + b[r])), x_c = the fc1 output
 // [5120] of clip c. Same K split and reduction order as gemv_residual_kernel<20> (thread t owns
-// 16-byte chunks t and t + 320 of every row, warp xor-tree, warps summed in order), with each weight
-// chunk read from shared memory once for all clips.
+// 16-byte chunks t and t + 320 of every row, warp xor-tree, warps summed in order). A CTA owns
+// kResidRows rows, bulk-copied into shared memory before the PDL wait; the clips are taken four at a
+// time with their x chunks converted to fp32 in registers once, each weight chunk converted once per
+// group and used for all four clips. Rows 0-7 of a group are reduced with warp_sum32_transpose.
 constexpr int kBfc2Threads = kResidThreads;  // 320
 
 struct BatchFc2Params {
@@ -2125,12 +2284,12 @@ struct BatchFc2Params {
   int clips;
 };
 
-__global__ void __launch_bounds__(kBfc2Threads) bfc2_residual_kernel(BatchFc2Params p) {
+__global__ void __launch_bounds__(kBfc2Threads, 1) bfc2_residual_kernel(BatchFc2Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ float red[kBfc2Threads / 32][kResidRows][kMaxClips];
-  constexpr int kc = kFfn / 8;                           // 640 chunks per row
-  constexpr int kPer = (kc + kBfc2Threads - 1) / kBfc2Threads;  // 2
+  static_assert(kResidRows == 10, "the transposed reduction covers rows 0-7, rows 8-9 use warp_sum");
+  constexpr int kc = kFfn / 8;  // 640 chunks per row; thread t owns chunks t and t + 320
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = blockIdx.x * kResidRows;
   const int C = p.clips;
@@ -2150,49 +2309,65 @@ __global__ void __launch_bounds__(kBfc2Threads) bfc2_residual_kernel(BatchFc2Par
   __syncthreads();
   pdl_wait();
   pdl_trigger();
-  uint4 xv[kMaxClips][kPer];
-#pragma unroll
-  for (int c = 0; c < kMaxClips; ++c) {
-    if (c >= C) break;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int ch = tid + kBfc2Threads * j;
-      xv[c][j] = ch < kc ? reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(c) * kFfn)[ch]
-                         : make_uint4(0, 0, 0, 0);
-    }
-  }
   const float hres = owner ? __half2float(p.h[static_cast<size_t>(oc) * kHidden + r0 + orow]) : 0.f;
-  if (!mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
+  bool waited = false;
 #pragma unroll 1
-  for (int r = 0; r < kResidRows; ++r) {
-    float acc[kMaxClips];
+  for (int c0 = 0; c0 < C; c0 += 4) {
+    float xf[4][2][8];
 #pragma unroll
-    for (int c = 0; c < kMaxClips; ++c) acc[c] = 0.f;
+    for (int cc = 0; cc < 4; ++cc) {
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int ch = tid + kBfc2Threads * j;
-      if (ch < kc) {
-        const uint4 wv = ws[r * kc + ch];
-        const half2* pw = reinterpret_cast<const half2*>(&wv);
+      for (int j = 0; j < 2; ++j) {
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (c0 + cc < C) xv = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(c0 + cc) * kFfn)[tid + 320 * j];
+        const half2* px = reinterpret_cast<const half2*>(&xv);
 #pragma unroll
-        for (int c = 0; c < kMaxClips; ++c) {
-          if (c >= C) break;
-          const half2* px = reinterpret_cast<const half2*>(&xv[c][j]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 fw = __half22float2(pw[e]), fx = __half22float2(px[e]);
-            acc[c] = fmaf(fw.x, fx.x, acc[c]);
-            acc[c] = fmaf(fw.y, fx.y, acc[c]);
-          }
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(px[e]);
+          xf[cc][j][2 * e] = f.x;
+          xf[cc][j][2 * e + 1] = f.y;
         }
       }
     }
-#pragma unroll
-    for (int c = 0; c < kMaxClips; ++c) {
-      if (c >= C) break;
-      const float a = warp_sum(acc[c]);
-      if (lane == 0) red[warp][r][c] = a;
+    if (!waited) {
+      if (!mbar_wait(&bar, 0)) flag_error(FW_DEVERR_TIMEOUT);
+      waited = true;
     }
+    float acc[32];  // rows 0-7 x clips 0-3, index 4 r + cc
+    float tail[2][4];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int r = 0; r < kResidRows; ++r) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint4 wv = ws[r * kc + tid + 320 * j];
+        const half2* pw = reinterpret_cast<const half2*>(&wv);
+        float wf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(pw[e]);
+          wf[2 * e] = f.x;
+          wf[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          float& a = r < 8 ? acc[4 * r + cc] : tail[r - 8][cc];
+          if (j == 0) a = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a = fmaf(wf[e], xf[cc][j][e], a);
+        }
+      }
+    }
+    const float s = warp_sum32_transpose(acc);  // lane l: row l / 4, clip c0 + l % 4
+    if (c0 + (lane & 3) < C) red[warp][lane >> 2][c0 + (lane & 3)] = s;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float t = warp_sum(tail[rr][cc]);
+        if (lane == 0 && c0 + cc < C) red[warp][8 + rr][c0 + cc] = t;
+      }
   }
   __syncthreads();
   if (owner) {
@@ -2201,6 +2376,23 @@ __global__ void __launch_bounds__(kBfc2Threads) bfc2_residual_kernel(BatchFc2Par
     for (int w = 0; w < kBfc2Threads / 32; ++w) sum += red[w][orow][oc];
     p.h[static_cast<size_t>(oc) * kHidden + r0 + orow] = __float2half(hres + round_half(sum + bias));
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// On-device decode loop (fw_decode_loop_*): the condition of a CUDA-graph WHILE node whose body is
+// decode steps. It replaces the host loop of custom/model.py:208-215 (replay an 8-step graph, read the
+// tokens back, stop at EOS or the token limit). ctrl (int64): [0] token limit, [1] EOS id,
+// [2] stop at EOS (0/1), [3] body iterations run, [4] iteration cap. The loop continues while fewer
+// than ctrl[0] tokens were generated, the last generated token is not EOS (when ctrl[2] is set) and
+// the cap is not reached (a guard that makes the loop finite whatever the state holds).
+__global__ void decode_loop_cond_kernel(const int64_t* __restrict__ state, const int64_t* __restrict__ tokens,
+                                        int64_t* __restrict__ ctrl, cudaGraphConditionalHandle handle, int first) {
+  const int64_t it = first ? 0 : ctrl[3] + 1;
+  ctrl[3] = it;
+  const int64_t n = state[1];
+  bool more = n < ctrl[0] && it < ctrl[4];
+  if (more && ctrl[2] != 0 && n > 0 && tokens[n - 1] == ctrl[1]) more = false;
+  cudaGraphSetConditional(handle, more ? 1u : 0u);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -2318,10 +2510,10 @@ static int launch_lm_head_q(LmParams p, cudaStream_t s, bool pdl) {
 template <int kAct, int kRowsPerWarp, bool kEmbed>
 static int launch_bln_gemv(const BatchGemvParams& p, cudaStream_t s) {
   auto kern = bln_gemv_kernel<kAct, kRowsPerWarp, kEmbed>;
-  constexpr int rows = 8 * kRowsPerWarp;
-  const int smem = rows * kHidden * 2 + p.clips * kHidden * 4;
-  cudaError_t e = ensure_smem(kern, rows * kHidden * 2 + kMaxClips * kHidden * 4);
-  if (e == cudaSuccess) e = launch(kern, dim3((p.n_out + rows - 1) / rows), dim3(256), smem, s, true, p);
+  using S = BlnShape<kRowsPerWarp>;
+  cudaError_t e = ensure_smem(kern, S::kSmem);
+  if (e == cudaSuccess)
+    e = launch(kern, dim3((p.n_out + S::kRows - 1) / S::kRows), dim3(kBlnThreads), S::kSmem, s, true, p);
   return launch_status(e, "batch_ln_gemv");
 }
 
@@ -2807,7 +2999,12 @@ int fw_decoder_step_trace(const fw_decoder_t* d, void* trace, fw_stream_t stream
   return decoder_one_step(d, static_cast<cudaStream_t>(stream), static_cast<half*>(trace));
 }
 
-int fw_batch_decoder_step(const fw_batch_decoder_t* d, int steps, fw_stream_t stream) {
+}  // extern "C"
+
+namespace fw {
+
+// Checks a batched decoder descriptor (fw_batch_decoder_step, fw_batch_decoder_launch).
+static int check_batch_decoder(const fw_batch_decoder_t* d) {
   FW_REQUIRE(d != nullptr, FW_ERR_NULL, "batch_decoder_step: descriptor is NULL");
   FW_REQUIRE(d->clips > 0 && d->clips <= kMaxClips, FW_ERR_SHAPE, "batch_decoder_step: clips must be 1..%d",
              kMaxClips);
@@ -2837,100 +3034,19 @@ int fw_batch_decoder_step(const fw_batch_decoder_t* d, int steps, fw_stream_t st
     FW_REQUIRE(aligned16(L.self_k) && aligned16(L.self_v) && aligned16(L.cross_k) && aligned16(L.cross_v),
                FW_ERR_ALIGN, "batch_decoder_step: caches must be 16-byte aligned");
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return FW_OK;
+}
+
+// Launch `block` of layer `l` of the batched step: 0 LN1 + q/k/v (layer 0: embedding), 1 self
+// attention, 2 out_proj + residual, 3 LN2 + cross q, 4 cross attention, 5 cross out_proj + residual,
+// 6 LN3 + fc1 + GELU, 7 fc2 + residual; block 8 (l ignored) is the LM head of all clips.
+static int batch_launch(const fw_batch_decoder_t* d, int l, int block, cudaStream_t s) {
   const int C = d->clips;
   half* h = static_cast<half*>(d->h);
   half* qkv = static_cast<half*>(d->qkv);
   half* attn = static_cast<half*>(d->attn);
   half* ffn = static_cast<half*>(d->ffn);
-  for (int step = 0; step < steps; ++step) {
-    for (int l = 0; l < d->n_layers; ++l) {
-      const fw_decoder_layer_t& L = d->layers[l];
-      int rc;
-      BatchGemvParams g{};
-      g.clips = C;
-      g.h = h;
-      g.eps = d->eps;
-      // LN1 + q/k/v (layer 0: h from the token embedding and position)
-      g.w = static_cast<const half*>(L.qkv_w);
-      g.b = static_cast<const half*>(L.qkv_b);
-      g.out = qkv;
-      g.n_out = 3 * kHidden;
-      g.out_stride = 3 * kHidden;
-      g.gamma = static_cast<const half*>(L.ln1_g);
-      g.beta = static_cast<const half*>(L.ln1_b);
-      g.embed = static_cast<const half*>(d->embed);
-      g.pos_embed = static_cast<const half*>(d->pos_embed);
-      g.cur = d->cur;
-      g.state = d->state;
-      g.prompt = d->prompt;
-      g.prompt_len = d->prompt_len;
-      g.vocab = d->vocab;
-      g.max_pos = d->max_pos;
-      g.h_out = h;
-      rc = l == 0 ? launch_bln_gemv<0, 3, true>(g, s) : launch_bln_gemv<0, 3, false>(g, s);
-      if (rc) return rc;
-      // self attention over position + 1 keys with the cache write, split combine fused
-      AttnParams a{};
-      a.q = qkv;
-      a.k = static_cast<half*>(L.self_k);
-      a.v = static_cast<half*>(L.self_v);
-      a.k_new = qkv + kHidden;
-      a.v_new = qkv + 2 * kHidden;
-      a.len_state = d->state;
-      a.max_len = d->max_pos;
-      a.scale = d->scale;
-      a.part_m = d->part_m;
-      a.part_l = d->part_l;
-      a.part_acc = d->part_acc;
-      a.out = attn;
-      a.counters = d->counters;
-      a.clip_q = 3 * kHidden;
-      a.clip_kv = d->self_clip_stride;
-      a.clip_new = 3 * kHidden;
-      a.clip_out = kHidden;
-      a.clip_state = 2;
-      cudaError_t e = launch(attn_split_kernel, dim3(d->heads, self_splits, C), dim3(64), 0, s, true, a);
-      if ((rc = launch_status(e, "batch_self_attention"))) return rc;
-      BatchOutParams o{static_cast<const half*>(L.out_w), static_cast<const half*>(L.out_b), attn, h, C};
-      if ((rc = launch_bout(o, s))) return rc;
-      // LN2 + cross q (into the q slot of qkv), cross attention, cross out_proj + residual
-      g.w = static_cast<const half*>(L.cq_w);
-      g.b = static_cast<const half*>(L.cq_b);
-      g.n_out = kHidden;
-      g.gamma = static_cast<const half*>(L.ln2_g);
-      g.beta = static_cast<const half*>(L.ln2_b);
-      if ((rc = launch_bln_gemv<0, 1, false>(g, s))) return rc;
-      AttnParams x{};
-      x.q = qkv;
-      x.k = const_cast<half*>(static_cast<const half*>(L.cross_k));
-      x.v = const_cast<half*>(static_cast<const half*>(L.cross_v));
-      x.max_len = d->enc_len;
-      x.scale = d->scale;
-      x.part_m = d->part_m;
-      x.part_l = d->part_l;
-      x.part_acc = d->part_acc;
-      x.out = attn;
-      x.counters = d->counters;
-      x.clip_q = 3 * kHidden;
-      x.clip_kv = d->cross_clip_stride;
-      x.clip_out = kHidden;
-      e = launch(attn_split_kernel, dim3(d->heads, cross_splits, C), dim3(64), 0, s, true, x);
-      if ((rc = launch_status(e, "batch_cross_attention"))) return rc;
-      BatchOutParams co{static_cast<const half*>(L.co_w), static_cast<const half*>(L.co_b), attn, h, C};
-      if ((rc = launch_bout(co, s))) return rc;
-      // LN3 + fc1 + GELU, fc2 + residual
-      g.w = static_cast<const half*>(L.fc1_w);
-      g.b = static_cast<const half*>(L.fc1_b);
-      g.out = ffn;
-      g.n_out = kFfn;
-      g.out_stride = kFfn;
-      g.gamma = static_cast<const half*>(L.ln3_g);
-      g.beta = static_cast<const half*>(L.ln3_b);
-      if ((rc = launch_bln_gemv<1, 4, false>(g, s))) return rc;
-      BatchFc2Params f{static_cast<const half*>(L.fc2_w), static_cast<const half*>(L.fc2_b), ffn, h, C};
-      if ((rc = launch_bfc2(f, s))) return rc;
-    }
+  if (block == 8) {
     LmParams m{};
     m.h = h;
     m.gamma = static_cast<const half*>(d->final_g);
@@ -2952,9 +3068,188 @@ int fw_batch_decoder_step(const fw_batch_decoder_t* d, int steps, fw_stream_t st
     m.max_pos = d->max_pos;
     m.prompt_len = d->prompt_len;
     m.clips = C;
-    int rc = launch_lm_head_q<true, true, kMaxClips>(m, s, true);
-    if (rc) return rc;
+    return launch_lm_head_q<true, true, kMaxClips>(m, s, true);
   }
+  const fw_decoder_layer_t& L = d->layers[l];
+  BatchGemvParams g{};
+  g.clips = C;
+  g.h = h;
+  g.eps = d->eps;
+  g.out = qkv;
+  g.out_stride = 3 * kHidden;
+  if (block == 0) {  // LN1 + q/k/v (layer 0: h from the token embedding and position)
+    g.w = static_cast<const half*>(L.qkv_w);
+    g.b = static_cast<const half*>(L.qkv_b);
+    g.n_out = 3 * kHidden;
+    g.gamma = static_cast<const half*>(L.ln1_g);
+    g.beta = static_cast<const half*>(L.ln1_b);
+    g.embed = static_cast<const half*>(d->embed);
+    g.pos_embed = static_cast<const half*>(d->pos_embed);
+    g.cur = d->cur;
+    g.state = d->state;
+    g.prompt = d->prompt;
+    g.prompt_len = d->prompt_len;
+    g.vocab = d->vocab;
+    g.max_pos = d->max_pos;
+    g.h_out = h;
+    return l == 0 ? launch_bln_gemv<0, 4, true>(g, s) : launch_bln_gemv<0, 4, false>(g, s);
+  }
+  if (block == 1 || block == 4) {  // self attention (cache write, fused combine) / cross attention
+    const bool self = block == 1;
+    AttnParams a{};
+    a.q = qkv;
+    a.k = const_cast<half*>(static_cast<const half*>(self ? L.self_k : L.cross_k));
+    a.v = const_cast<half*>(static_cast<const half*>(self ? L.self_v : L.cross_v));
+    if (self) {
+      a.k_new = qkv + kHidden;
+      a.v_new = qkv + 2 * kHidden;
+      a.len_state = d->state;
+      a.clip_new = 3 * kHidden;
+      a.clip_state = 2;
+    }
+    a.max_len = self ? d->max_pos : d->enc_len;
+    a.scale = d->scale;
+    a.part_m = d->part_m;
+    a.part_l = d->part_l;
+    a.part_acc = d->part_acc;
+    a.out = attn;
+    a.counters = d->counters;
+    a.clip_q = 3 * kHidden;
+    a.clip_kv = self ? d->self_clip_stride : d->cross_clip_stride;
+    a.clip_out = kHidden;
+    const int splits = (a.max_len + kSplitKeys - 1) / kSplitKeys;
+    cudaError_t e = launch(attn_split_kernel, dim3(d->heads, splits, C), dim3(64), 0, s, true, a);
+    return launch_status(e, self ? "batch_self_attention" : "batch_cross_attention");
+  }
+  if (block == 2 || block == 5) {  // (cross) out_proj + residual
+    BatchOutParams o{static_cast<const half*>(block == 2 ? L.out_w : L.co_w),
+                     static_cast<const half*>(block == 2 ? L.out_b : L.co_b), attn, h, C};
+    return launch_bout(o, s);
+  }
+  if (block == 3) {  // LN2 + cross q (into the q slot of qkv)
+    g.w = static_cast<const half*>(L.cq_w);
+    g.b = static_cast<const half*>(L.cq_b);
+    g.n_out = kHidden;
+    g.gamma = static_cast<const half*>(L.ln2_g);
+    g.beta = static_cast<const half*>(L.ln2_b);
+    return launch_bln_gemv<0, 2, false>(g, s);
+  }
+  if (block == 6) {  // LN3 + fc1 + GELU
+    g.w = static_cast<const half*>(L.fc1_w);
+    g.b = static_cast<const half*>(L.fc1_b);
+    g.out = ffn;
+    g.n_out = kFfn;
+    g.out_stride = kFfn;
+    g.gamma = static_cast<const half*>(L.ln3_g);
+    g.beta = static_cast<const half*>(L.ln3_b);
+    return launch_bln_gemv<1, 5, false>(g, s);
+  }
+  BatchFc2Params f{static_cast<const half*>(L.fc2_w), static_cast<const half*>(L.fc2_b), ffn, h, C};
+  return launch_bfc2(f, s);
+}
+
+}  // namespace fw
+
+extern "C" {
+
+int fw_batch_decoder_step(const fw_batch_decoder_t* d, int steps, fw_stream_t stream) {
+  int rc = check_batch_decoder(d);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int step = 0; step < steps; ++step) {
+    for (int l = 0; l < d->n_layers; ++l)
+      for (int block = 0; block < 8; ++block)
+        if ((rc = batch_launch(d, l, block, s))) return rc;
+    if ((rc = batch_launch(d, 0, 8, s))) return rc;
+  }
+  return FW_OK;
+}
+
+int fw_batch_decoder_launch(const fw_batch_decoder_t* d, int layer, int block, fw_stream_t stream) {
+  int rc = check_batch_decoder(d);
+  if (rc) return rc;
+  FW_REQUIRE(block >= 0 && block <= 8, FW_ERR_ARG, "batch_decoder_launch: block must be 0..8");
+  FW_REQUIRE(block == 8 || (layer >= 0 && layer < d->n_layers), FW_ERR_ARG, "batch_decoder_launch: layer out of range");
+  return batch_launch(d, block == 8 ? 0 : layer, block, static_cast<cudaStream_t>(stream));
+}
+
+struct fw_decode_loop {
+  cudaGraph_t graph;
+  cudaGraphExec_t exec;
+};
+
+int fw_decode_loop_create(const fw_decoder_t* d, int64_t* ctrl, int steps_per_iter, fw_decode_loop_t** out) {
+  int rc = check_decoder(d);
+  if (rc) return rc;
+  FW_REQUIRE(ctrl != nullptr && out != nullptr, FW_ERR_NULL, "decode_loop_create: ctrl and out are required");
+  FW_REQUIRE(steps_per_iter >= 1 && steps_per_iter <= 64, FW_ERR_SHAPE, "decode_loop_create: steps_per_iter must be 1..64");
+  *out = nullptr;
+  cudaGraph_t graph = nullptr, body = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaStream_t s = nullptr;
+  cudaGraphConditionalHandle handle;
+  cudaGraphNode_t init_node = nullptr, loop_node = nullptr;
+  cudaError_t e = cudaGraphCreate(&graph, 0);
+  if (e == cudaSuccess) e = cudaGraphConditionalHandleCreate(&handle, graph, 0, 0);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  // node 1: the condition for the first iteration
+  if (e == cudaSuccess) e = cudaStreamBeginCaptureToGraph(s, graph, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed);
+  if (e == cudaSuccess) {
+    decode_loop_cond_kernel<<<1, 1, 0, s>>>(static_cast<const int64_t*>(d->state), static_cast<const int64_t*>(d->tokens),
+                                           ctrl, handle, 1);
+    e = cudaGetLastError();
+    cudaError_t e2 = cudaStreamEndCapture(s, &graph);
+    if (e == cudaSuccess) e = e2;
+  }
+  if (e == cudaSuccess) {
+    size_t n = 1;
+    e = cudaGraphGetNodes(graph, &init_node, &n);
+  }
+  // node 2: WHILE(handle) { steps_per_iter decode steps; condition }
+  if (e == cudaSuccess) {
+    cudaGraphNodeParams cp = {};
+    cp.type = cudaGraphNodeTypeConditional;
+    cp.conditional.handle = handle;
+    cp.conditional.type = cudaGraphCondTypeWhile;
+    cp.conditional.size = 1;
+    e = cudaGraphAddNode(&loop_node, graph, &init_node, 1, &cp);
+    if (e == cudaSuccess) body = cp.conditional.phGraph_out[0];
+  }
+  if (e == cudaSuccess) e = cudaStreamBeginCaptureToGraph(s, body, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed);
+  if (e == cudaSuccess) {
+    for (int i = 0; i < steps_per_iter && rc == FW_OK; ++i) rc = decoder_one_step(d, s, nullptr);
+    if (rc == FW_OK) {
+      decode_loop_cond_kernel<<<1, 1, 0, s>>>(static_cast<const int64_t*>(d->state),
+                                             static_cast<const int64_t*>(d->tokens), ctrl, handle, 0);
+      e = cudaGetLastError();
+    }
+    cudaError_t e2 = cudaStreamEndCapture(s, &body);
+    if (e == cudaSuccess) e = e2;
+  }
+  if (e == cudaSuccess && rc == FW_OK) e = cudaGraphInstantiate(&exec, graph, 0);
+  if (s) cudaStreamDestroy(s);
+  if (rc != FW_OK || e != cudaSuccess) {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (rc != FW_OK) return rc;
+    return set_error(FW_ERR_LAUNCH, "decode_loop_create: %s", cudaGetErrorString(e));
+  }
+  fw_decode_loop_t* loop = new fw_decode_loop_t{graph, exec};
+  *out = loop;
+  return FW_OK;
+}
+
+int fw_decode_loop_launch(fw_decode_loop_t* loop, fw_stream_t stream) {
+  FW_REQUIRE(loop != nullptr, FW_ERR_NULL, "decode_loop_launch: loop is NULL");
+  cudaError_t e = cudaGraphLaunch(loop->exec, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FW_OK : set_error(FW_ERR_LAUNCH, "decode_loop_launch: %s", cudaGetErrorString(e));
+}
+
+int fw_decode_loop_destroy(fw_decode_loop_t* loop) {
+  if (loop == nullptr) return FW_OK;
+  cudaGraphExecDestroy(loop->exec);
+  cudaGraphDestroy(loop->graph);
+  delete loop;
   return FW_OK;
 }
 

@@ -268,6 +268,11 @@ class Ext:
         """`steps` decode steps of every clip of a batched decoder descriptor (_lib.BatchDecoder)."""
         _lib.call('fw_batch_decoder_step', ctypes.byref(desc), int(steps), _stream())
 
+    def batch_decoder_launch(self, desc, layer, block):
+        """One launch of the batched step (0 qkv, 1 self attention, 2 out_proj, 3 cross q, 4 cross
+        attention, 5 cross out_proj, 6 fc1, 7 fc2, 8 LM head)."""
+        _lib.call('fw_batch_decoder_launch', ctypes.byref(desc), int(layer), int(block), _stream())
+
     def decoder_launch(self, desc, layer, block):
         """One launch of the decode step (block 0 self, 1 cross, 2 fc1, 3 fc2, 4 LM head)."""
         _lib.call('fw_decoder_launch', ctypes.byref(desc), int(layer), int(block), _stream())

@@ -135,6 +135,7 @@ class CustomModel:
         self.enc_out = torch.zeros(T, d, dtype=half, device=dev)
         self.evt = torch.zeros(d, -(-T // 8) * 8, dtype=half, device=dev)  # V^T of the encoder attention
         self.tokens_host = torch.zeros(self.max_pos, dtype=torch.long).pin_memory()
+        self._wave_copied = None  # event after the last asynchronous copy out of wave_host
 
         self.dec_desc = self._decoder_desc()
         self.enc_desc = self._encoder_desc()
@@ -142,6 +143,7 @@ class CustomModel:
         if selftest:
             self.selftest['mel_max_abs_diff'] = self._mel_diff()
         self.graph_mel = self.graph_enc = self.graph_prompt = self.graph_chunk = None
+        self.loop = None
         if capture:
             self._capture()
 
@@ -272,6 +274,44 @@ class CustomModel:
             self.selftest['encoder_graph_max_abs_diff'] = float((self.enc_out.float() - eager.float()).abs().max())
             self.selftest['encoder_graph'] = True
             self.mel.copy_(mel_saved)
+        self._make_loop()
+
+    def _make_loop(self, steps_per_iter=1):
+        """The on-device decode loop (fw_decode_loop_*): one graph launch decodes until EOS or the token
+        limit, the stop condition evaluated on the GPU after every step."""
+        self.loop_ctrl = torch.zeros(5, dtype=torch.long, device='cuda')
+        self.loop_ctrl_host = torch.zeros(5, dtype=torch.long).pin_memory()
+        self._ctrl_copied = None
+        handle = ctypes.c_void_p()
+        try:
+            _lib.call('fw_decode_loop_create', ctypes.byref(self.dec_desc), _p(self.loop_ctrl), int(steps_per_iter),
+                      ctypes.byref(handle))
+            self.loop = handle
+            self.selftest['decode_loop'] = True
+        except RuntimeError as exc:  # the host loop of chunk graphs is used instead
+            self.loop = None
+            self.selftest['decode_loop'] = False
+            self.selftest['decode_loop_error'] = str(exc)
+
+    def __del__(self):
+        loop = getattr(self, 'loop', None)
+        if loop is not None:
+            _lib.lib().fw_decode_loop_destroy(loop)
+            self.loop = None
+
+    def run_loop(self, limit, stop_at_eos, eos=None):
+        """Decode steps on the GPU until state[1] (tokens generated) reaches `limit` or, with
+        stop_at_eos, the last generated token is `eos` (default: the model's EOS id); one graph
+        launch, no host synchronisation."""
+        if self._ctrl_copied is not None:
+            self._ctrl_copied.synchronize()
+        eos = self.dims.eos_token_id if eos is None else int(eos)
+        self.loop_ctrl_host.copy_(torch.tensor([int(limit), eos, int(bool(stop_at_eos)), 0,
+                                                self.max_pos + len(self.prompt)]))
+        self.loop_ctrl.copy_(self.loop_ctrl_host, non_blocking=True)
+        self._ctrl_copied = torch.cuda.Event()
+        self._ctrl_copied.record()
+        _lib.call('fw_decode_loop_launch', self.loop, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
     def run_mel(self):
         self.graph_mel.replay() if self.graph_mel else self._mel()
@@ -291,11 +331,17 @@ class CustomModel:
 
     @torch.inference_mode()
     def load_audio(self, audio):
-        """Copies a host clip (zero-padded to 30 s) into the device waveform buffer."""
+        """Copies a host clip (zero-padded to 30 s) into the device waveform buffer. The copy from the
+        pinned staging buffer is asynchronous; the staging buffer is rewritten only after the previous
+        copy from it has completed."""
+        if self._wave_copied is not None:
+            self._wave_copied.synchronize()
         host = self.wave_host.numpy()
         host[:audio.size] = audio
         host[audio.size:] = 0.0
         self.wave.copy_(self.wave_host, non_blocking=True)
+        self._wave_copied = torch.cuda.Event()
+        self._wave_copied.record()
 
     def run_steps(self, n):
         """n decode steps: whole CHUNK-step graphs, then the remainder launched directly."""
@@ -321,22 +367,30 @@ class CustomModel:
         if not 0 < audio.size <= N_SAMPLES or not np.isfinite(audio).all():
             raise ValueError('audio must contain finite samples and be between 0 and 30 seconds')
 
-    def batch_decoder(self):
-        """The batched decoder (flash_whisper_b200.batch.BatchDecoder, 8 clips), created on first use."""
+    def batch_decoders(self):
+        """The two batched decoders (flash_whisper_b200.batch.BatchDecoder, 8 clips each) that
+        transcribe_batch alternates between, created on first use."""
         if getattr(self, '_batch', None) is None:
             from .batch import BatchDecoder
-            self._batch = BatchDecoder(self)
-            self.waves_host = torch.zeros(self._batch.clips, N_SAMPLES, dtype=torch.float32).pin_memory()
+            self._batch = [BatchDecoder(self), BatchDecoder(self)]
         return self._batch
+
+    def batch_decoder(self):
+        """The first batched decoder (8 clips per weight read)."""
+        return self.batch_decoders()[0]
 
     @torch.inference_mode()
     def transcribe_batch(self, audios, max_new_tokens=None, stop_at_eos=True):
-        """Transcribes several clips, up to 8 per decoder weight read (flash_whisper_b200.batch).
+        """Transcribes several clips with the batched decoder (flash_whisper_b200.batch): 8 clips per
+        decoder weight read, the encoders of the next 8 clips overlapping the current decode.
 
         Returns one dict per clip with transcribe()'s keys; each clip's token ids are exactly those
-        transcribe() returns for it alone. `max_new_tokens` is one limit or one per clip. Clips are
-        taken in the given order, 8 at a time; the stage times of a clip are those of its pass
-        (log-mel and encoder of every clip of the pass, then their joint decode)."""
+        transcribe() returns for it alone. `max_new_tokens` is one limit or one per clip; clips are
+        grouped in the given order (give them longest first to waste the fewest steps). A group is
+        decoded to its longest limit and every clip is then cut at its limit and, with stop_at_eos, at
+        its first EOS. Times: mel_s / encoder_s are the clip's own device times; ttft_s, ttlt_s and
+        e2e_s are those of the whole call, whose decode_s is its wall time minus the clip's front end."""
+        from .batch import run_clips
         for a in audios:
             self._check_audio(a)
         n_all = len(audios)
@@ -344,57 +398,27 @@ class CustomModel:
             limits = [min(int(x), self.max_new) for x in max_new_tokens]
         else:
             limits = [self.max_new if max_new_tokens is None else min(int(max_new_tokens), self.max_new)] * n_all
-        bd = self.batch_decoder()
-        stream = torch.cuda.current_stream()
+        decoders = self.batch_decoders()
+        if getattr(self, '_staging', None) is None:
+            from .batch import HostStaging
+            self._staging = HostStaging(2 * decoders[0].clips, N_SAMPLES)
+        torch.cuda.synchronize()
+        start = time.perf_counter()
+        tokens, times = run_clips(self, decoders, None, limits, host_audio=audios, staging=self._staging)
+        ttlt = time.perf_counter() - start
+        rows = tokens.tolist()
         results = []
-        for g0 in range(0, n_all, bd.clips):
-            group, lim = audios[g0:g0 + bd.clips], limits[g0:g0 + bd.clips]
-            n, steps = len(group), max(lim)
-            torch.cuda.synchronize()
-            start = time.perf_counter()
-            hw = self.waves_host.numpy()
-            for c, a in enumerate(group):
-                hw[c, :a.size] = a
-                hw[c, a.size:] = 0.0
-            ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
-            for c in range(n):
-                ev[c][0].record(stream)
-                self.wave.copy_(self.waves_host[c], non_blocking=True)
-                self.run_mel()
-                ev[c][1].record(stream)
-                bd.encoder_slot(c)
-                ev[c][2].record(stream)
-            if steps - 1 >= bd.chunk:
-                bd._chunk_graph(n)
-            bd.prompt(n)
-            first_done = torch.cuda.Event()
-            first_done.record(stream)
-            first_done.synchronize()
-            ttft = time.perf_counter() - start
-            done = 1
-            while done < steps:
-                k = min(bd.chunk, steps - done)
-                bd.steps(n, k)
-                done += k
-                if stop_at_eos:
-                    toks = bd.tokens[:n, :done].cpu().tolist()
-                    if all(any(t in self.eos for t in row[:lim[c]]) or done >= lim[c] for c, row in enumerate(toks)):
-                        break
-            toks = bd.tokens[:n, :done].cpu().tolist()
-            ttlt = time.perf_counter() - start
-            mel_s = [e[0].elapsed_time(e[1]) / 1e3 for e in ev]
-            enc_s = [e[1].elapsed_time(e[2]) / 1e3 for e in ev]
-            for c in range(n):
-                ids = toks[c][:lim[c]]
-                if stop_at_eos:
-                    cut = next((i + 1 for i, t in enumerate(ids) if t in self.eos), len(ids))
-                    ids = ids[:cut]
-                d0 = time.perf_counter()
-                text = self.tokenizer.decode(ids, skip_special_tokens=True)
-                results.append({'text': text, 'token_ids': ids, 'ttft_s': ttft, 'ttlt_s': ttlt,
-                                'e2e_s': time.perf_counter() - start, 'mel_s': mel_s[c], 'encoder_s': enc_s[c],
-                                'decode_s': ttlt - sum(mel_s) - sum(enc_s), 'detok_s': time.perf_counter() - d0,
-                                'n_tokens': len(ids), 'batch': n})
+        for i in range(n_all):
+            ids = rows[i][:limits[i]]
+            if stop_at_eos:
+                cut = next((k + 1 for k, t in enumerate(ids) if t in self.eos), len(ids))
+                ids = ids[:cut]
+            d0 = time.perf_counter()
+            text = self.tokenizer.decode(ids, skip_special_tokens=True)
+            results.append({'text': text, 'token_ids': ids, 'ttft_s': ttlt, 'ttlt_s': ttlt,
+                            'e2e_s': time.perf_counter() - start, 'mel_s': times[i][0], 'encoder_s': times[i][1],
+                            'decode_s': ttlt - times[i][0] - times[i][1], 'detok_s': time.perf_counter() - d0,
+                            'n_tokens': len(ids)})
         return results
 
     @torch.inference_mode()
@@ -425,6 +449,21 @@ class CustomModel:
             ttft = time.perf_counter() - start
             stream.synchronize()
             token_ids = self.tokens_host[:limit].tolist()
+        elif self.loop is not None:
+            # prompt -> first token read back (TTFT) while the on-device loop decodes to EOS / limit
+            self.tokens_host[:1].copy_(self.tokens[:1], non_blocking=True)
+            first = torch.cuda.Event()
+            first.record(stream)
+            self.run_loop(limit, True)
+            self.tokens_host[:limit].copy_(self.tokens[:limit], non_blocking=True)
+            state_host = self.state.to('cpu', non_blocking=True)
+            first.synchronize()
+            ttft = time.perf_counter() - start
+            stream.synchronize()
+            n = min(int(state_host[1]), limit)
+            token_ids = self.tokens_host[:n].tolist()
+            cut = next((i + 1 for i, t in enumerate(token_ids) if t in self.eos), len(token_ids))
+            token_ids = token_ids[:cut]
         else:
             done_events = []
             issued = 0

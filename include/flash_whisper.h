@@ -218,6 +218,27 @@ int fw_decoder_launch(const fw_decoder_t* d, int layer, int block, fw_stream_t s
 int fw_decoder_step_trace(const fw_decoder_t* d, void* trace, fw_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
+ * On-device decode loop: one CUDA graph whose WHILE node runs decode steps until a clip is done,
+ * with the stop condition evaluated on the GPU. Replaces the host loop of custom/model.py:208-215
+ * (replay an 8-step graph, copy the tokens back, check for EOS on the host) with one graph launch.
+ * ---------------------------------------------------------------------------------------- */
+typedef struct fw_decode_loop fw_decode_loop_t;
+
+/* Builds the loop for decoder `d` (pointers are baked into the graph: d's buffers must stay
+ * allocated while the loop exists). ctrl is a device int64[5] that the caller fills before each
+ * launch: ctrl[0] = token limit (stop once state[1] reaches it), ctrl[1] = EOS id, ctrl[2] = 1 to stop
+ * after the first EOS token (0 to ignore EOS), ctrl[4] = cap on body iterations (a guard; the loop
+ * always ends); ctrl[3] receives the number of body iterations run minus one. Each iteration runs
+ * `steps_per_iter` decode steps, then re-evaluates the condition; the condition is also evaluated
+ * once before the first iteration. Host-side set-up only: it creates (and destroys) a private
+ * stream and the graph, and launches nothing. */
+int fw_decode_loop_create(const fw_decoder_t* d, int64_t* ctrl, int steps_per_iter, fw_decode_loop_t** out);
+/* Launches the loop on `stream` (asynchronous; one graph launch). */
+int fw_decode_loop_launch(fw_decode_loop_t* loop, fw_stream_t stream);
+/* Frees the graph (NULL is accepted). */
+int fw_decode_loop_destroy(fw_decode_loop_t* loop);
+
+/* ------------------------------------------------------------------------------------------
  * Batched decode step: up to FW_MAX_CLIPS independent clips per weight read (no reference
  * counterpart: the reference decodes one clip per step, custom/model.py:107-123). Each clip's
  * arithmetic is exactly the batch-1 step's, so its tokens equal decoding it alone with
@@ -251,6 +272,12 @@ typedef struct {
  * cross attention, cross out_proj + residual, LN3 + fc1 + GELU, fc2 + residual; then the pruned LM
  * head of all clips with the final LN, argmax and bookkeeping (33 launches per step). */
 int fw_batch_decoder_step(const fw_batch_decoder_t* d, int steps, fw_stream_t stream);
+
+/* One launch of the batched step in isolation, as fw_batch_decoder_step issues it (for per-kernel
+ * timing and profiling): block 0 = LN1 + q/k/v of `layer`, 1 = self attention, 2 = out_proj +
+ * residual, 3 = LN2 + cross q, 4 = cross attention, 5 = cross out_proj + residual, 6 = LN3 + fc1 +
+ * GELU, 7 = fc2 + residual, 8 = LM head of all clips (`layer` ignored). */
+int fw_batch_decoder_launch(const fw_batch_decoder_t* d, int layer, int block, fw_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * GPU log-mel front end (custom/model.py:93-98; WhisperFeatureExtractor semantics)

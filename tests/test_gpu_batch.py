@@ -80,3 +80,19 @@ def test_batched_descriptor_checks(model, batch):
     ctypes_copy.lm_q = None
     with pytest.raises(RuntimeError, match='required pointer'):
         model.ext.batch_decoder_step(ctypes_copy, 1)
+
+
+@torch.inference_mode()
+def test_transcribe_batch_pipeline_equals_transcribe(model):
+    """transcribe_batch (two batched decoders on two streams, encoders of the next group overlapping
+    the current decode, a partial last group) returns for every clip what transcribe() returns."""
+    rng = np.random.default_rng(11)
+    secs = sorted((float(rng.uniform(5.0, 30.0)) for _ in range(11)), reverse=True)
+    audios = [synthetic_audio(200 + i, s) for i, s in enumerate(secs)]
+    limits = [int(round(7.5 * s)) // 4 for s in secs]
+    outs = model.transcribe_batch(audios, max_new_tokens=limits, stop_at_eos=False)
+    assert len(outs) == len(audios)
+    for i, (a, lim) in enumerate(zip(audios, limits)):
+        want = model.transcribe(a, max_new_tokens=lim, stop_at_eos=False)['token_ids']
+        assert outs[i]['token_ids'] == want, f'clip {i}'
+        assert outs[i]['n_tokens'] == lim
