@@ -351,12 +351,16 @@ class CustomModel:
             self.ext.decoder_step(self.dec_desc, n % self.chunk)
 
     @torch.inference_mode()
-    def decode_device(self, n_tokens):
+    def decode_device(self, n_tokens, loop=False):
         """Device-resident pipeline after the waveform is in self.wave: front, prompt (which yields
-        the first token) and exactly n_tokens - 1 further decode steps."""
+        the first token) and exactly n_tokens - 1 further decode steps, as chunk-graph replays or
+        (loop=True) one launch of the on-device decode loop."""
         self.run_front()
         self.run_prompt()
-        self.run_steps(max(0, n_tokens - 1))
+        if loop and self.loop is not None:
+            self.run_loop(n_tokens, False)
+        else:
+            self.run_steps(max(0, n_tokens - 1))
 
     # ---- public API --------------------------------------------------------------------------
     @staticmethod
