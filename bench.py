@@ -34,8 +34,9 @@ kernels compiled from source, HF fp16 encoder, cuBLAS projections, its CUDA grap
 package on the same GPU, weights and audio, and the reference kernels beside this package's on the
 config-1 microbench inputs.
 
---workload profile --tokens N (a profiler target) runs one transcription eagerly: log-mel, encoder,
-prompt and N decode steps, one launch after another.
+--workload profile --tokens N [--batched M] (a profiler target) runs one transcription eagerly: log-mel,
+encoder, prompt and N decode steps, one launch after another; then M batched decode steps of 8 clips
+inside the NVTX range `batched`. --lean keeps only the config-3 measurements (for ncu launch lists).
 """
 
 import argparse
@@ -609,8 +610,8 @@ def bench_ours(args, rank, world, local_rank):
     pk = peaks()
     kernels = decode_kernel_table(model, dims, pk)
     dominant = max(kernels, key=lambda k: kernels[k]['share'])
-    micro = micro_table(model, dims, pk) if rank == 0 else None
-    c4 = config4(args, model, dims, ranks, rank, world, pk)
+    micro = micro_table(model, dims, pk) if rank == 0 and not args.lean else None
+    c4 = config4(args, model, dims, ranks, rank, world, pk) if not args.lean else None
 
     avg_len = 4 + N_TOKENS // 2
     pruned = model.lm_q is not None
@@ -774,6 +775,19 @@ def profile_run(args):
         model.ext.decoder_step(model.dec_desc, 1)
     torch.cuda.synchronize()
     print('tokens', model.tokens[:args.tokens + 1].tolist())
+    if args.batched:
+        from flash_whisper_b200.batch import BatchDecoder
+        bd = BatchDecoder(model)
+        for c in range(bd.clips):
+            model.load_audio(synthetic_audio(c, 20.0))
+            model._mel()
+            model.ext.encoder_forward(bd.enc_descs[c])
+        bd.prompt(bd.clips)
+        torch.cuda.nvtx.range_push('batched')  # lets a profiler select the batched steps
+        model.ext.batch_decoder_step(bd._desc(bd.clips), args.batched)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        print('batched tokens', bd.tokens[:, :bd.clips].tolist())
     return 0
 
 
@@ -786,6 +800,10 @@ def main():
     parser.add_argument('--no-cpu-baseline', action='store_true')
     parser.add_argument('--workload', choices=('clip30', 'refcuda', 'profile'), default='clip30')
     parser.add_argument('--tokens', type=int, default=4, help='decode steps of --workload profile')
+    parser.add_argument('--batched', type=int, default=0,
+                        help='--workload profile: also this many batched decode steps of 8 clips')
+    parser.add_argument('--lean', action='store_true',
+                        help='config-3 line only: no config-1/2 microbench and no config-4 run (profiler runs)')
     args = parser.parse_args()
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
