@@ -81,50 +81,6 @@ __device__ __forceinline__ float ln_apply(float v, float mean, float inv, float 
   return fmaf((v - mean) * inv, g, b);
 }
 
-// ln1280_stats of the first C of kClips rows at once (two barriers for all of them): every row's
-// statistics are formed in exactly ln1280_stats' order. red: kClips x 16 floats of shared memory.
-template <int kClips>
-__device__ __forceinline__ void ln1280_stats_clips(const float (&v)[kClips][5], float (*red)[16], int C, float eps,
-                                                   float (&mean)[kClips], float (&inv)[kClips]) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int c = 0; c < kClips; ++c) {
-    if (c >= C) break;
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 5; ++i) sum += v[c][i];
-    sum = warp_sum(sum);
-    if (lane == 0) red[c][warp] = sum;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < kClips; ++c) {
-    if (c >= C) break;
-    float m = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m += red[c][i];
-    m /= static_cast<float>(kHidden);
-    mean[c] = m;
-    float sq = 0.f;
-#pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const float d = v[c][i] - m;
-      sq = fmaf(d, d, sq);
-    }
-    sq = warp_sum(sq);
-    if (lane == 0) red[c][8 + warp] = sq;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < kClips; ++c) {
-    if (c >= C) break;
-    float var = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) var += red[c][8 + i];
-    inv[c] = rsqrtf(var / static_cast<float>(kHidden) + eps);
-  }
-}
-
 // Dot product of one 1280-wide fp16 row (16-byte chunks lane + 32*c) with x held as 40 floats per
 // lane in the same chunk order. The fma order is the reference LM-head order (whisper_kernels.cu:58-68).
 __device__ __forceinline__ float dot1280_lane(const uint4* row, const float (&xf)[40]) {
@@ -1204,13 +1160,14 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ float red[16];
-  __shared__ float red_clips[kClips][16];
+  __shared__ float ln_g[kClips > 1 ? kHidden : 1], ln_b[kClips > 1 ? kHidden : 1];  // final LN (several clips)
   __shared__ __align__(16) float4 rps[kLmMaxRowsPerCta];
   __shared__ uint8_t msk[2][kLmMaxRowsPerCta];
   __shared__ float warp_l[kClips][8], warp_b[kClips][8], xstat[kClips][2][8];
   __shared__ unsigned long long warp_best[kClips][8];
   __shared__ int ncand[kClips];
   __shared__ unsigned s_lo_max[kClips];  // running max of the lower bounds (order-preserving bits)
+  __shared__ unsigned s_b_max[kClips];   // several clips: max of the bounds (order-preserving bits)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* stages = smem_raw + (base - raw);
@@ -1262,6 +1219,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   if (threadIdx.x < kClips) {
     ncand[threadIdx.x] = 0;
     s_lo_max[threadIdx.x] = float_to_ordered(-INFINITY);
+    s_b_max[threadIdx.x] = float_to_ordered(0.f);
   }
   float g[5], be[5];
   if (kLN) {
@@ -1269,6 +1227,10 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
     for (int i = 0; i < 5; ++i) {
       g[i] = __half2float(p.gamma[threadIdx.x + i * 256]);
       be[i] = __half2float(p.beta[threadIdx.x + i * 256]);
+      if (kClips > 1) {
+        ln_g[threadIdx.x + i * 256] = g[i];
+        ln_b[threadIdx.x + i * 256] = be[i];
+      }
     }
   }
   tc_fence_before();
@@ -1278,66 +1240,52 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   pdl_wait();
   pdl_trigger();
 
-  // LayerNorm of each clip's row (ln1280_stats order; consecutive calls may share `red`), its
-  // max|x| and |x|_1, and the B operand rows 2c (x_hi) and 2c + 1 (x_lo) of xq = rint(x / sx).
-  float xv[kClips][5];
-  if constexpr (kClips > 1) {
+  // LayerNorm of each clip's row, its max|x| and |x|_1, and the B operand rows 2c (x_hi) and 2c + 1
+  // (x_lo) of xq = rint(x / sx). 16-byte unit j of row n of an 8-row 128B-swizzled atom is stored at
+  // unit j ^ (n % 8); rows 8..15 form the second atom of the K chunk.
+  auto put_b = [&](int n, int k, int val) {
+    const int ch = k >> 7, kk = k & 127;
+    xb[ch * S::kN * kQChunk + (n >> 3) * 1024 + (n & 7) * kQChunk + ((((kk >> 4) ^ (n & 7)) & 7) << 4) + (kk & 15)] =
+        static_cast<uint8_t>(static_cast<int8_t>(val));
+  };
+  auto put_xq = [&](int c, int k, float x, float xinv) {
+    const int xq = max(-8191, min(8191, __float2int_rn(x * xinv)));
+    const int xh = (xq + 64) >> 7;  // floor((xq + 64) / 128), in [-64, 64]
+    put_b(2 * c, k, xh);
+    put_b(2 * c + 1, k, xq - (xh << 7));  // in [-64, 63]
+  };
+  float sx[kClips], nx1[kClips];
+  if constexpr (kClips == 1) {
+    // all 256 threads on the one row, ln1280_stats order
+    float xv[5];
     if (kLN) {
-      float mean[kClips], inv[kClips];
 #pragma unroll
-      for (int c = 0; c < kClips; ++c) {
-        if (c >= C) break;
-#pragma unroll
-        for (int i = 0; i < 5; ++i) xv[c][i] = __half2float(p.h[c * kHidden + threadIdx.x + i * 256]);
-      }
-      ln1280_stats_clips<kClips>(xv, red_clips, C, p.eps, mean, inv);
-#pragma unroll
-      for (int c = 0; c < kClips; ++c) {
-        if (c >= C) break;
-#pragma unroll
-        for (int i = 0; i < 5; ++i) {
-          const half y = __float2half(ln_apply(xv[c][i], mean[c], inv[c], g[i], be[i]));
-          ys[c * kHidden + threadIdx.x + i * 256] = y;
-          xv[c][i] = __half2float(y);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < kClips; ++c) {
-    if (c >= C) break;
-    const half* hc = p.h + c * kHidden;
-    half* yc = ys + c * kHidden;
-    if (kLN && kClips > 1) {
-      // normalised above
-    } else if (kLN) {
-#pragma unroll
-      for (int i = 0; i < 5; ++i) xv[c][i] = __half2float(hc[threadIdx.x + i * 256]);
+      for (int i = 0; i < 5; ++i) xv[i] = __half2float(p.h[threadIdx.x + i * 256]);
       float mean, inv;
-      ln1280_stats(xv[c], red, p.eps, mean, inv);
+      ln1280_stats(xv, red, p.eps, mean, inv);
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
-        const half y = __float2half(ln_apply(xv[c][i], mean, inv, g[i], be[i]));
-        yc[threadIdx.x + i * 256] = y;
-        xv[c][i] = __half2float(y);
+        const half y = __float2half(ln_apply(xv[i], mean, inv, g[i], be[i]));
+        ys[threadIdx.x + i * 256] = y;
+        xv[i] = __half2float(y);
       }
     } else {
 #pragma unroll
       for (int i = 0; i < 5; ++i) {
-        const half y = hc[threadIdx.x + i * 256];
-        yc[threadIdx.x + i * 256] = y;
-        xv[c][i] = __half2float(y);
+        const half y = p.h[threadIdx.x + i * 256];
+        ys[threadIdx.x + i * 256] = y;
+        xv[i] = __half2float(y);
       }
     }
-    if (kClips == 1 && p.y_out && blockIdx.x == 0) {
+    if (p.y_out && blockIdx.x == 0) {
 #pragma unroll
-      for (int i = 0; i < 5; ++i) p.y_out[threadIdx.x + i * 256] = __float2half(xv[c][i]);
+      for (int i = 0; i < 5; ++i) p.y_out[threadIdx.x + i * 256] = __float2half(xv[i]);
     }
     float mx = 0.f, sm = 0.f;
 #pragma unroll
     for (int i = 0; i < 5; ++i) {
-      mx = fmaxf(mx, fabsf(xv[c][i]));
-      sm += fabsf(xv[c][i]);
+      mx = fmaxf(mx, fabsf(xv[i]));
+      sm += fabsf(xv[i]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1345,45 +1293,107 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
       sm += __shfl_xor_sync(0xffffffffu, sm, o);
     }
     if (lane == 0) {
-      xstat[c][0][warp] = mx;
-      xstat[c][1][warp] = sm;
+      xstat[0][0][warp] = mx;
+      xstat[0][1][warp] = sm;
     }
-  }
-  __syncthreads();
-  float sx[kClips], nx1[kClips];
-#pragma unroll
-  for (int c = 0; c < kClips; ++c) {
+    __syncthreads();
     float xmax = 0.f, n1 = 0.f;
-    if (c < C) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        xmax = fmaxf(xmax, xstat[c][0][i]);
-        n1 += xstat[c][1][i];
-      }
+    for (int i = 0; i < 8; ++i) {
+      xmax = fmaxf(xmax, xstat[0][0][i]);
+      n1 += xstat[0][1][i];
     }
-    nx1[c] = n1 * 1.0001f;  // covers the fp32 rounding of the sum
-    sx[c] = xmax > 0.f ? xmax / kXqMax : 0.f;
+    nx1[0] = n1 * 1.0001f;  // covers the fp32 rounding of the sum
+    sx[0] = xmax > 0.f ? xmax / kXqMax : 0.f;
     const float xinv = xmax > 0.f ? kXqMax / xmax : 0.f;
-    if (c >= C) continue;
-    // B operand: 16-byte unit j of row n of an 8-row 128B-swizzled atom is stored at unit j ^ (n % 8);
-    // rows 8..15 form the second atom of the K chunk.
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const int k = threadIdx.x + i * 256;
-      const int xq = max(-8191, min(8191, __float2int_rn(xv[c][i] * xinv)));
-      const int xh = (xq + 64) >> 7;  // floor((xq + 64) / 128), in [-64, 64]
-      const int xl = xq - (xh << 7);  // in [-64, 63]
-      const int ch = k >> 7, kk = k & 127;
-      uint8_t* chunk = xb + ch * S::kN * kQChunk;
-      const int n0 = 2 * c, n1r = 2 * c + 1;
-      chunk[(n0 >> 3) * 1024 + (n0 & 7) * kQChunk + ((((kk >> 4) ^ (n0 & 7)) & 7) << 4) + (kk & 15)] =
-          static_cast<uint8_t>(static_cast<int8_t>(xh));
-      chunk[(n1r >> 3) * 1024 + (n1r & 7) * kQChunk + ((((kk >> 4) ^ (n1r & 7)) & 7) << 4) + (kk & 15)] =
-          static_cast<uint8_t>(static_cast<int8_t>(xl));
+    for (int i = 0; i < 5; ++i) put_xq(0, threadIdx.x + i * 256, xv[i], xinv);
+  } else {
+    // Warp w normalises clip w by itself. Its 32 lanes stand in for the 256 threads of ln1280_stats
+    // one warp-row at a time (virtual warp j = threads 32j .. 32j + 31), so the per-thread sums, the
+    // xor-trees and the ordered sum of the eight warp partials are exactly ln1280_stats'. The code is
+    // one short loop per clip rather than eight unrolled copies. (|x|_1 only scales a bound, which
+    // the 1.0001 factor keeps rigorous in any summation order.)
+    const int c = warp;
+    if (c < C) {
+      const half* hc = p.h + c * kHidden;
+      half* yc = ys + c * kHidden;
+      float v[8][5];
+      float part[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 5; ++i) {
+          v[j][i] = __half2float(hc[32 * j + lane + 256 * i]);
+          sum += v[j][i];
+        }
+        part[j] = warp_sum(sum);
+      }
+      if (kLN) {
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m += part[j];
+        m /= static_cast<float>(kHidden);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float sq = 0.f;
+#pragma unroll
+          for (int i = 0; i < 5; ++i) {
+            const float d = v[j][i] - m;
+            sq = fmaf(d, d, sq);
+          }
+          part[j] = warp_sum(sq);
+        }
+        float var = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) var += part[j];
+        const float inv = rsqrtf(var / static_cast<float>(kHidden) + p.eps);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int i = 0; i < 5; ++i) {
+            const int k = 32 * j + lane + 256 * i;
+            const half y = __float2half(ln_apply(v[j][i], m, inv, ln_g[k], ln_b[k]));
+            yc[k] = y;
+            v[j][i] = __half2float(y);
+          }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int i = 0; i < 5; ++i) yc[32 * j + lane + 256 * i] = __float2half(v[j][i]);
+      }
+      float mx = 0.f, sm = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int i = 0; i < 5; ++i) {
+          mx = fmaxf(mx, fabsf(v[j][i]));
+          sm += fabsf(v[j][i]);
+        }
+      mx = warp_max(mx);
+      sm = warp_sum(sm);
+      const float xinv = mx > 0.f ? kXqMax / mx : 0.f;
+      if (lane == 0) {
+        xstat[c][0][0] = mx > 0.f ? mx / kXqMax : 0.f;
+        xstat[c][1][0] = sm * 1.0001f;  // covers the fp32 rounding of the sum
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int i = 0; i < 5; ++i) put_xq(c, 32 * j + lane + 256 * i, v[j][i], xinv);
     }
   }
   fence_proxy_async_shared();  // B written by the generic proxy, read by the tensor core
   __syncthreads();
+  if constexpr (kClips > 1) {
+#pragma unroll
+    for (int c = 0; c < kClips; ++c) {
+      sx[c] = c < C ? xstat[c][0][0] : 0.f;
+      nx1[c] = c < C ? xstat[c][1][0] : 0.f;
+    }
+  }
 
   const uint8_t* maskc[kClips];
 #pragma unroll
@@ -1488,9 +1498,15 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
         if constexpr (kClips == 1) {
           run = live ? fmaxf(ordered_to_float(atomicMax(&s_lo_max[c], float_to_ordered(lo))), lo) : lo;
         } else {
+          // (s_lo_max then ends as this CTA's maximum lower bound of the clip, T; the bound
+          // maximum goes to s_b_max the same way, so no reduction is left after the loop)
           const float wlo = warp_max(lo);
+          const float wb = warp_max(live ? ((!isfinite(approx) || !isfinite(b)) ? INFINITY : b) : 0.f);
           unsigned prev = 0;
-          if (lane == 0) prev = atomicMax(&s_lo_max[c], float_to_ordered(wlo));
+          if (lane == 0) {
+            prev = atomicMax(&s_lo_max[c], float_to_ordered(wlo));
+            atomicMax(&s_b_max[c], float_to_ordered(wb));
+          }
           prev = __shfl_sync(0xffffffffu, prev, 0);
           run = fmaxf(ordered_to_float(prev), wlo);
         }
@@ -1499,36 +1515,48 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
       if (fetch) l2_prefetch(p.w + static_cast<size_t>(r0 + li) * kHidden, kHidden * 2);
     }
   }
-#pragma unroll
-  for (int c = 0; c < kClips; ++c) {
+  if constexpr (kClips == 1) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      lmax[c] = fmaxf(lmax[c], __shfl_xor_sync(0xffffffffu, lmax[c], o));
-      bmax[c] = fmaxf(bmax[c], __shfl_xor_sync(0xffffffffu, bmax[c], o));
+      lmax[0] = fmaxf(lmax[0], __shfl_xor_sync(0xffffffffu, lmax[0], o));
+      bmax[0] = fmaxf(bmax[0], __shfl_xor_sync(0xffffffffu, bmax[0], o));
     }
     if (lane == 0) {
-      warp_l[c][warp] = lmax[c];
-      warp_b[c][warp] = bmax[c];
+      warp_l[0][warp] = lmax[0];
+      warp_b[0][warp] = bmax[0];
     }
   }
   __syncthreads();
 
   // ---- row selection per clip: U_r >= T - m (every row when the bound is unusable) ----
-#pragma unroll
-  for (int c = 0; c < kClips; ++c) {
-    if (c >= C) break;
+  if constexpr (kClips == 1) {
     float t = -INFINITY, bm = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      t = fmaxf(t, warp_l[c][i]);
-      bm = fmaxf(bm, warp_b[c][i]);
+      t = fmaxf(t, warp_l[0][i]);
+      bm = fmaxf(bm, warp_b[0][i]);
     }
     const bool all_rows = !(fabsf(t) < 32768.f) || !(bm < 32768.f);
     const float thr = t - (0x1p-9f * (fabsf(t) + 2.f * bm) + 0x1p-23f);
     for (int i = threadIdx.x; i < nrows; i += 256) {
-      if (!maskc[c][i] && (all_rows || ub[c * kLmMaxRowsPerCta + i] >= thr))
-        cand[c * kLmMaxRowsPerCta + atomicAdd(&ncand[c], 1)] = static_cast<unsigned short>(i);
+      if (!maskc[0][i] && (all_rows || ub[i] >= thr)) cand[atomicAdd(&ncand[0], 1)] = static_cast<unsigned short>(i);
     }
+  } else if (warp < C) {  // warp w selects clip w's rows, compacted with a ballot (no atomics)
+    const int c = warp;
+    const float t = ordered_to_float(s_lo_max[c]), bm = ordered_to_float(s_b_max[c]);
+    const bool all_rows = !(fabsf(t) < 32768.f) || !(bm < 32768.f);
+    const float thr = t - (0x1p-9f * (fabsf(t) + 2.f * bm) + 0x1p-23f);
+    const uint8_t* mk = (kFinalize && p.first_mask && p.prompt_len > 0 && p.state[2 * c] == p.prompt_len - 1)
+                            ? msk[1] : msk[0];
+    int n = 0;
+    for (int i0 = 0; i0 < nrows; i0 += 32) {
+      const int i = i0 + lane;
+      const bool take = i < nrows && !mk[i] && (all_rows || ub[c * kLmMaxRowsPerCta + i] >= thr);
+      const unsigned bal = __ballot_sync(0xffffffffu, take);
+      if (take) cand[c * kLmMaxRowsPerCta + n + __popc(bal & ((1u << lane) - 1u))] = static_cast<unsigned short>(i);
+      n += __popc(bal);
+    }
+    if (lane == 0) ncand[c] = n;
   }
   __syncthreads();
 
@@ -1539,8 +1567,8 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
 #pragma unroll
     for (int c = 0; c < kClips; ++c) warp_best[c][warp] = 0ull;  // this warp's entry of every clip
   }
-#pragma unroll 1
-  for (int c = (kClips == 1 ? 0 : warp); c < (kClips == 1 ? C : min(C, warp + 1)); ++c) {
+  if (kClips == 1 || warp < C) {
+    const int c = kClips == 1 ? 0 : warp;
     float xf[40];
     load_x40(ys + c * kHidden, xf);
     const int nc = ncand[c];
