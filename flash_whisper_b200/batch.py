@@ -189,9 +189,10 @@ class HostStaging:
 def run_clips(model, decoders, waves, n_tokens, host_audio=None, staging=None):
     """Decodes many clips through two batched decoders on two CUDA streams.
 
-    Clips are taken in order, `decoders[0].clips` at a time (group g uses decoders[g % 2]). On the
-    front-end stream the log-mel and encoder of every clip of group g+1 run while the decode stream
-    decodes group g, so the tensor-core encoder overlaps the memory-bound decode. waves: device
+    Clips are taken in order, `decoders[0].clips` at a time (group g uses decoders[g % 2], each decoder
+    on its own stream). On the front-end stream the log-mel and encoders of the next groups run while
+    the two decode streams decode the current ones, so the tensor-core encoder and two latency-bound
+    decodes share the GPU. waves: device
     float32 [n, 480000], or None with host_audio (float32 numpy clips, copied in on the front-end
     stream through `staging`, a HostStaging). Returns the token tensor [n, max_pos] on the host (clip
     i's tokens in its first n_tokens[i] entries) and per-clip (log-mel, encoder) device times in s.
@@ -205,9 +206,11 @@ def run_clips(model, decoders, waves, n_tokens, host_audio=None, staging=None):
         if len(grp) != clips:
             decoders[g % 2].prepare(len(grp))
     cur = torch.cuda.current_stream()
-    front, back = torch.cuda.Stream(), torch.cuda.Stream()
+    front = torch.cuda.Stream()
+    backs = [torch.cuda.Stream() for _ in decoders]  # decoder g % 2 decodes on its own stream
     front.wait_stream(cur)
-    back.wait_stream(cur)
+    for b in backs:
+        b.wait_stream(cur)
     tokens = torch.zeros(n_all, model.max_pos, dtype=torch.long).pin_memory()
     enc_done = [torch.cuda.Event() for _ in groups]
     dec_done = [torch.cuda.Event() for _ in groups]
@@ -228,13 +231,15 @@ def run_clips(model, decoders, waves, n_tokens, host_audio=None, staging=None):
                 bd.encoder_slot(c)
                 stage_ev[i][2].record(front)
             enc_done[g].record(front)
+        back = backs[g % len(backs)]
         with torch.cuda.stream(back):
             back.wait_event(enc_done[g])
             bd.decode(len(grp), max(n_tokens[i] for i in grp))
             tokens[grp[0]:grp[-1] + 1].copy_(bd.tokens[:len(grp)], non_blocking=True)
             dec_done[g].record(back)
     cur.wait_stream(front)
-    cur.wait_stream(back)
+    for b in backs:
+        cur.wait_stream(b)
     torch.cuda.synchronize()
     times = [(e[0].elapsed_time(e[1]) / 1e3, e[1].elapsed_time(e[2]) / 1e3) for e in stage_ev]
     return tokens, times
