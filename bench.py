@@ -496,8 +496,8 @@ def config4(args, model, dims, ranks, rank, world, pk):
     bk, step_us = batch_kernel_table(model, bd, dims, pk)
     batched = {
         'decoder': f'fw_batch_decoder_step, {bd.clips} clips per weight read, groups of consecutive clips of the '
-                   'longest-first partition, tokens identical to the batch-1 path; two decoders on two streams, '
-                   'the log-mel + encoders of group g+1 overlapping the decode of group g',
+                   'longest-first partition, tokens identical to the batch-1 path; three decoders on three '
+                   'streams beside the log-mel + encoder stream',
         'kernels': bk, 'step_us_sum_of_kernels': round(step_us, 2),
         'whole_box_audio_s_per_s': round(total_audio / (b_max / 1e3), 2),
         'e2e_audio_s_per_s': round(total_audio / b_e2e_s, 2),

@@ -187,12 +187,12 @@ class HostStaging:
 
 @torch.inference_mode()
 def run_clips(model, decoders, waves, n_tokens, host_audio=None, staging=None):
-    """Decodes many clips through two batched decoders on two CUDA streams.
+    """Decodes many clips through several batched decoders, each on its own CUDA stream.
 
-    Clips are taken in order, `decoders[0].clips` at a time (group g uses decoders[g % 2], each decoder
-    on its own stream). On the front-end stream the log-mel and encoders of the next groups run while
-    the two decode streams decode the current ones, so the tensor-core encoder and two latency-bound
-    decodes share the GPU. waves: device
+    Clips are taken in order, `decoders[0].clips` at a time (group g uses decoders[g % len(decoders)],
+    each decoder on its own stream). On the front-end stream the log-mel and encoders of the next
+    groups run while the decode streams decode the current ones, so the tensor-core encoder and
+    several latency-bound decodes share the GPU. waves: device
     float32 [n, 480000], or None with host_audio (float32 numpy clips, copied in on the front-end
     stream through `staging`, a HostStaging). Returns the token tensor [n, max_pos] on the host (clip
     i's tokens in its first n_tokens[i] entries) and per-clip (log-mel, encoder) device times in s.
@@ -204,10 +204,10 @@ def run_clips(model, decoders, waves, n_tokens, host_audio=None, staging=None):
         bd.prepare(clips)
     for g, grp in enumerate(groups):
         if len(grp) != clips:
-            decoders[g % 2].prepare(len(grp))
+            decoders[g % len(decoders)].prepare(len(grp))
     cur = torch.cuda.current_stream()
     front = torch.cuda.Stream()
-    backs = [torch.cuda.Stream() for _ in decoders]  # decoder g % 2 decodes on its own stream
+    backs = [torch.cuda.Stream() for _ in decoders]  # each decoder decodes on its own stream
     front.wait_stream(cur)
     for b in backs:
         b.wait_stream(cur)
@@ -215,11 +215,12 @@ def run_clips(model, decoders, waves, n_tokens, host_audio=None, staging=None):
     enc_done = [torch.cuda.Event() for _ in groups]
     dec_done = [torch.cuda.Event() for _ in groups]
     stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_all)]
+    nd = len(decoders)
     for g, grp in enumerate(groups):
-        bd = decoders[g % 2]
+        bd = decoders[g % nd]
         with torch.cuda.stream(front):
-            if g >= 2:
-                front.wait_event(dec_done[g - 2])  # the slot set of group g - 2 is free again
+            if g >= nd:
+                front.wait_event(dec_done[g - nd])  # the slot set of group g - nd is free again
             for c, i in enumerate(grp):
                 stage_ev[i][0].record(front)
                 if waves is not None:

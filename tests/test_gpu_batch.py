@@ -84,7 +84,7 @@ def test_batched_descriptor_checks(model, batch):
 
 @torch.inference_mode()
 def test_transcribe_batch_pipeline_equals_transcribe(model):
-    """transcribe_batch (two batched decoders on two streams, encoders of the next group overlapping
+    """transcribe_batch (three batched decoders on three streams, encoders of the next groups overlapping
     the current decode, a partial last group) returns for every clip what transcribe() returns."""
     rng = np.random.default_rng(11)
     secs = sorted((float(rng.uniform(5.0, 30.0)) for _ in range(11)), reverse=True)
