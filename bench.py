@@ -66,9 +66,13 @@ CONFIG3 = {'workload': 'BASELINE config 3: GPU log-mel + graphed 32-layer encode
            'seq_len': N_TOKENS, 'l2': 'working set larger than L2 (282 MB per decode step, 1.26 GB encoder weights)'}
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the ncu captures in profiles/
-# (decode_attention_blocks.txt, decode_fc1_fc2.txt, lm_head_q_decode_step.txt)
-NCU_TRAFFIC = {'self_block': 13_180_928, 'cross_block': 14_283_776, 'fc1': 13_154_560, 'fc2': 13_139_200,
-               'lm_head': 76_108_032 + 1_145_088}
+# (decode_attention_blocks.txt, decode_fc1_fc2.txt, lm_head_q_decode_step.txt, batched_decode_step.txt)
+NCU_TRAFFIC = {'self_block': 13_180_672, 'cross_block': 14_285_568, 'fc1': 13_154_304, 'fc2': 13_139_712,
+               'lm_head': 77_523_968}
+# the batched capture's self attention runs at length 5, not the table's 116: no traffic figure for it
+BATCH_NCU_TRAFFIC = {'qkv': 9_908_480, 'self_attention': None, 'out_proj': 3_346_688, 'cross_q': 3_344_384,
+                     'cross_attention': 61_842_432, 'cross_out_proj': 3_346_944, 'fc1': 13_209_088,
+                     'fc2': 13_238_016, 'lm_head': 77_309_184}
 
 
 def peaks():
@@ -360,7 +364,8 @@ def batch_kernel_table(model, bd, dims, pk, length=116):
         us = graph_us(lambda: ext.batch_decoder_launch(desc, layer, block))
         gbs = nbytes[key] / (us * 1e-6) / 1e9
         table[key] = {'us': round(us, 3), 'bytes': nbytes[key], 'gbs': round(gbs, 1),
-                      'frac': round(gbs / pk['hbm_gbs'], 4), 'launches_per_step': 1 if key == 'lm_head' else 4}
+                      'frac': round(gbs / pk['hbm_gbs'], 4), 'launches_per_step': 1 if key == 'lm_head' else 4,
+                      'ncu_traffic': BATCH_NCU_TRAFFIC[key]}
     total = sum(v['us'] * v['launches_per_step'] for v in table.values())
     for v in table.values():
         v['share'] = round(v['us'] * v['launches_per_step'] / total, 4)
@@ -766,7 +771,8 @@ def profile_run(args):
     from flash_whisper_b200.audio import synthetic_audio
     from flash_whisper_b200.model import CustomModel
     from flash_whisper_b200.weights import TURBO, random_state_dict
-    model = CustomModel(state_dict=random_state_dict(0, TURBO), dims=TURBO, selftest=False, capture=False)
+    model = CustomModel(state_dict=random_state_dict(0, TURBO), dims=TURBO, selftest=False, capture=False,
+                        lm_prune=not args.lm_fp16)
     model.load_audio(synthetic_audio(0, SECONDS))
     model._mel()
     model._encode()
@@ -775,7 +781,7 @@ def profile_run(args):
         model.ext.decoder_step(model.dec_desc, 1)
     torch.cuda.synchronize()
     print('tokens', model.tokens[:args.tokens + 1].tolist())
-    if args.batched:
+    if args.batched and model.lm_q is not None:
         from flash_whisper_b200.batch import BatchDecoder
         bd = BatchDecoder(model)
         for c in range(bd.clips):
@@ -802,6 +808,8 @@ def main():
     parser.add_argument('--tokens', type=int, default=4, help='decode steps of --workload profile')
     parser.add_argument('--batched', type=int, default=0,
                         help='--workload profile: also this many batched decode steps of 8 clips')
+    parser.add_argument('--lm-fp16', action='store_true',
+                        help='--workload profile: the full fp16 LM head (lm_head_kernel) instead of the pruned one')
     parser.add_argument('--lean', action='store_true',
                         help='config-3 line only: no config-1/2 microbench and no config-4 run (profiler runs)')
     args = parser.parse_args()
