@@ -75,11 +75,21 @@ __device__ __forceinline__ float ordered_to_float(unsigned int u) {
 // Programmatic dependent launch. A kernel launched with the PDL attribute may start while the
 // previous kernel in the stream is still running. Before pdl_wait() it may only read data that
 // no in-flight kernel writes (weights, caches written by earlier steps); pdl_wait() blocks until
-// the previous grid has completed and its memory is visible. Every kernel here calls
-// pdl_trigger() only after its own pdl_wait(), so at most two grids overlap and the pre-wait
-// region of grid N never races with grid N-2.
+// the previous grid has completed and its memory is visible (and so, transitively, every grid
+// before it). Most kernels here call pdl_trigger() only after their own pdl_wait(); the decode
+// step's fc1 and fc2 GEMVs call it before, so up to four of its grids overlap. That is safe because
+// every pre-wait region of the decode step reads only weights, the cross cache and self-cache rows
+// of earlier steps, and the position, whose last writer (the previous step's LM head) completed
+// before any attention block released its successor.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// GPU-scope fetch-add with acquire-release semantics (one round trip: no separate fences).
+__device__ __forceinline__ unsigned atomic_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 // ---------------------------------------------------------------------------------------------
 // mbarrier + bulk copy (1-D TMA) helpers.

@@ -568,9 +568,8 @@ struct HeadBlockShape {
   static constexpr int kProjBytes = kProjRows * kHidden * 2;
   static constexpr int kKvBytes = kUnits * 2 * kSplitKeys * kHeadDim * 2;
   static constexpr int kOutBytes = kOutRows * kHeadDim * 2;
-  // the output-projection slice reuses the projection rows' buffer once step 1 is done
-  static constexpr int kWBytes = kProjBytes > kOutBytes ? kProjBytes : kOutBytes;
-  static constexpr int kSmem = kWBytes + kKvBytes;
+  // projection rows | K/V splits | output-projection slice, all requested before the PDL wait
+  static constexpr int kSmem = kProjBytes + kKvBytes + kOutBytes;
 };
 
 template <bool kSelf, bool kEmbed>
@@ -596,8 +595,8 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   const int heads = gridDim.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   half* wproj = reinterpret_cast<half*>(smem);
-  half* kvs = reinterpret_cast<half*>(smem + S::kWBytes);
-  half* wout = wproj;  // reused after step 1
+  half* kvs = reinterpret_cast<half*>(smem + S::kProjBytes);
+  half* wout = reinterpret_cast<half*>(smem + S::kProjBytes + S::kKvBytes);
   const int splits = (p.kv_len + kSplitKeys - 1) / kSplitKeys;
   half* kh = p.k + static_cast<size_t>(head) * p.kv_len * kHeadDim;
   half* vh = p.v + static_cast<size_t>(head) * p.kv_len * kHeadDim;
@@ -656,9 +655,9 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
         }
       }
     }
-    // the output-projection slice is copied into shared memory after step 1; warm it in L2 now
-    l2_prefetch_hint(p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes,
-                     stream_policy);
+    mbar_arrive_expect_tx(&bar_o, S::kOutBytes);
+    bulk_g2s_stream(wout, p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes,
+                    &bar_o, stream_policy);
   }
   // LayerNorm parameters and biases are weights: loaded before the wait, into registers
   constexpr int kRowsPerWarp = (S::kProjRows + 7) / 8;
@@ -728,12 +727,6 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   // otherwise queue in front of this kernel's loads of h, and this kernel runs long enough after
   // this point for that prefetch to complete.
   pdl_trigger();
-  if (tid == 0) {  // every thread of this CTA is past its reads of the projection rows
-    fence_proxy_async_shared();
-    mbar_arrive_expect_tx(&bar_o, S::kOutBytes);
-    bulk_g2s_stream(wout, p.wo + (static_cast<size_t>(head) * kHidden + rank * kOutRows) * kHeadDim, S::kOutBytes,
-                    &bar_o, stream_policy);
-  }
 
   // ---- 2. attention splits ----
   {
@@ -829,14 +822,10 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   }
 
   // ---- 5. residual update by the last CTA of this row block ----
-  // Release/acquire through thread 0 (the barrier orders the CTA's partial stores before its fence).
+  // Thread 0's acq_rel arrival releases the CTA's partial stores (ordered before it by the barrier)
+  // and, in the last CTA, acquires every other CTA's; the second barrier extends that to its threads.
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const bool last = atomicAdd(p.counter + rank, 1u) == static_cast<unsigned>(heads - 1);
-    if (last) __threadfence();
-    s_last = last;
-  }
+  if (tid == 0) s_last = atomic_add_acq_rel(p.counter + rank, 1u) == static_cast<unsigned>(heads - 1);
   __syncthreads();
   if (!s_last) return;
   if (tid < kOutRows) {
@@ -1746,8 +1735,10 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
     bias[i] = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
   }
   __syncthreads();
-  pdl_wait();
+  // Released before the wait: the next launch (fc2 in the decode step) reads only weights before its
+  // own wait, so it may start its weight copies while the launch before this one still runs.
   pdl_trigger();
+  pdl_wait();
 
   float v[5];
 #pragma unroll
@@ -1795,8 +1786,8 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
 // length k = 256 * kChunks. The CTA splits k, not rows: thread t owns 16-byte chunks t, t + 320, ...
 // of x (in registers) and of every row, accumulates one partial per row, and the partials are summed
 // over each warp (xor tree) and then over the warps in order, so each weight and x byte is read
-// from shared memory once. The weight rows are bulk-copied and the bias and residual entries loaded
-// before the PDL wait: the previous launch must not write h (in the decode step fc2 follows fc1).
+// from shared memory once. The weight rows are bulk-copied and the bias loaded before the PDL wait,
+// the residual entries after it.
 constexpr int kResidRows = 10;  // 1280 / 10 = 128 CTAs: no SM holds two, leaving room for the next launch
 constexpr int kResidThreads = 320;
 
@@ -1825,10 +1816,12 @@ __global__ void __launch_bounds__(kResidThreads) gemv_residual_kernel(GemvParams
   }
   const bool owner = tid < nr;  // thread r finishes row r
   const float bias = (p.b && owner) ? __half2float(p.b[r0 + tid]) : 0.f;
-  const float hres = owner ? __half2float(p.h_res[r0 + tid]) : 0.f;
   __syncthreads();
-  pdl_wait();
+  // Released before the wait (the next decode launch reads only weights, and cache rows of earlier
+  // steps, before its own wait); the residual is read after it.
   pdl_trigger();
+  pdl_wait();
+  const float hres = owner ? __half2float(p.h_res[r0 + tid]) : 0.f;
   uint4 xv[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {

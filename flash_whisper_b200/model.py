@@ -287,6 +287,7 @@ class CustomModel:
             _lib.call('fw_decode_loop_create', ctypes.byref(self.dec_desc), _p(self.loop_ctrl), int(steps_per_iter),
                       ctypes.byref(handle))
             self.loop = handle
+            self._loop_destroy = _lib.lib().fw_decode_loop_destroy  # held: module globals may be gone at exit
             self.selftest['decode_loop'] = True
         except RuntimeError as exc:  # the host loop of chunk graphs is used instead
             self.loop = None
@@ -294,9 +295,9 @@ class CustomModel:
             self.selftest['decode_loop_error'] = str(exc)
 
     def __del__(self):
-        loop = getattr(self, 'loop', None)
-        if loop is not None:
-            _lib.lib().fw_decode_loop_destroy(loop)
+        loop, destroy = getattr(self, 'loop', None), getattr(self, '_loop_destroy', None)
+        if loop is not None and destroy is not None:
+            destroy(loop)
             self.loop = None
 
     def run_loop(self, limit, stop_at_eos, eos=None):
