@@ -173,6 +173,47 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
+// Shared::cluster address of `p` (this CTA's shared memory) in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_map(const void* p, unsigned rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// Asynchronous stores into another cluster CTA's shared memory (addresses from cluster_map); the bytes
+// are counted on the receiving CTA's mbarrier `rbar`, whose waiters then see them. The receiver must
+// have initialised the mbarrier before (a completed cluster barrier phase) and must not exit before
+// its wait on it completes.
+__device__ __forceinline__ void st_async_b32(uint32_t raddr, uint32_t v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr), "r"(v),
+               "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, uint4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   raddr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rbar)
+               : "memory");
+}
+// Bounded wait (cluster-scope acquire) on a phase completed by other CTAs' st.async bytes.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, unsigned parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      unsigned ok;
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(ok)
+          : "r"(smem_u32(bar)), "r"(parity)
+          : "memory");
+      if (ok) return true;
+    }
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

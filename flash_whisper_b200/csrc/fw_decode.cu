@@ -272,10 +272,13 @@ __device__ __forceinline__ void unit_sync(int id) {
 // reference's per-warp residue classes (keys i = r mod 4, r = 0..3) and their final order, so the
 // partial (m, l, acc) is bit-identical to the reference kernel's while the score pass no longer
 // serialises a shuffle reduction per key. K rows are read with a per-thread chunk rotation so the
-// 16-byte shared loads are bank-conflict free. part_* may point into another CTA's shared memory.
+// 16-byte shared loads are bank-conflict free. With kCopies > 1, part_* are this CTA's shared arrays
+// and the partial is sent to the same slots of every CTA of the cluster by st.async, counted on
+// their mbarrier `xbar` (264 bytes per CTA).
 template <int kCopies = 1>
 __device__ __forceinline__ void attn_unit64(const half* ks, const half* vs, int n, float scale, int t, SplitScratch& U,
-                                            int sync_id, float* part_acc, float* part_m, float* part_l) {
+                                            int sync_id, float* part_acc, float* part_m, float* part_l,
+                                            uint64_t* xbar = nullptr) {
   const int lane = t & 31, wa = t >> 5;
   float s = -INFINITY;
   if (t < n) {
@@ -354,14 +357,21 @@ __device__ __forceinline__ void attn_unit64(const half* ks, const half* vs, int 
       *part_m = m;
       *part_l = l;
     }
-  } else {  // part_* are this CTA's shared arrays; the same slot is written in every CTA of the cluster
-    cg::cluster_group cluster = cg::this_cluster();
+  } else {  // the same slots in every CTA of the cluster: this CTA's by plain stores
+    const unsigned own = cg::this_cluster().block_rank();
+    part_acc[t] = a;
+    if (t == 0) {
+      *part_m = m;
+      *part_l = l;
+    }
 #pragma unroll
     for (int r = 0; r < kCopies; ++r) {
-      cluster.map_shared_rank(part_acc, r)[t] = a;
+      if (r == static_cast<int>(own)) continue;
+      const uint32_t rb = cluster_map(xbar, r);
+      st_async_b32(cluster_map(part_acc + t, r), __float_as_uint(a), rb);
       if (t == 0) {
-        *cluster.map_shared_rank(part_m, r) = m;
-        *cluster.map_shared_rank(part_l, r) = l;
+        st_async_b32(cluster_map(part_m, r), __float_as_uint(m), rb);
+        st_async_b32(cluster_map(part_l, r), __float_as_uint(l), rb);
       }
     }
   }
@@ -520,8 +530,9 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
 //      arrival counter per block, nothing spins) sums the per-head partials in head order, adds the
 //      bias and the residual: h[r] = fp16(h[r] + fp16(sum + b[r])).
 // Weight rows, the K/V splits and the output-projection slice (head-major [heads, 1280, 64]) are
-// bulk-copied into shared memory before griddepcontrol.wait. Only two cluster barriers are needed,
-// after which no CTA touches another CTA's shared memory.
+// bulk-copied into shared memory before griddepcontrol.wait. The two exchanges inside the cluster
+// (projection rows, split partials) are st.async stores counted on the receiving CTA's mbarrier, so
+// a CTA waits only for the bytes it needs, not for every CTA to reach a cluster barrier.
 constexpr int kHeads = kHidden / kHeadDim;                // 20
 constexpr int kHeadCtas = 8;                              // CTAs per head cluster
 constexpr int kHeadMaxUnits = 3;                          // attention splits per CTA (cross: 24 / 8)
@@ -577,6 +588,7 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   using S = HeadBlockShape<kSelf>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar_w, bar_kv, bar_o;
+  __shared__ __align__(8) uint64_t bar_x, bar_s;  // DSMEM exchanges: projection rows, split partials
   __shared__ float red[16];
   __shared__ __align__(16) half ys[kHidden];
   __shared__ __align__(16) half hs[kHidden];                   // residual-stream input (for step 5)
@@ -589,7 +601,6 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   __shared__ float sm_w[S::kSlots];
   __shared__ int s_last;
 
-  cg::cluster_group cluster = cg::this_cluster();
   const int rank = blockIdx.x;  // cluster dims (kHeadCtas, 1, 1) over grid (kHeadCtas, heads)
   const int head = blockIdx.y;
   const int heads = gridDim.y;
@@ -622,7 +633,10 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     mbar_init(&bar_w, 1);
     mbar_init(&bar_kv, 1);
     mbar_init(&bar_o, 1);
+    mbar_init(&bar_x, 1);
+    mbar_init(&bar_s, 1);
     mbar_fence_init();
+    mbar_arrive_expect_tx(&bar_x, (kHeadCtas - 1) * S::kProjRows * 2);  // the other CTAs' rows
     mbar_arrive_expect_tx(&bar_w, S::kProjBytes);
     for (int r = 0; r < S::kProjRows; ++r)
       bulk_g2s_stream(wproj + r * kHidden, p.w + static_cast<size_t>(proj_row(rank * S::kProjRows + r)) * kHidden,
@@ -686,6 +700,12 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     pos = static_cast<int>(min(max(raw, int64_t(0)), int64_t(p.max_pos - 1)));
     len = pos + 1;
   }
+  if (tid == 0) {  // partials of the other CTAs' splits: 66 floats each, (m, l) alone for an empty split
+    unsigned sb = 0;
+    for (int sp = 0; sp < splits; ++sp)
+      if (sp / S::kUnits != rank) sb += (len - sp * kSplitKeys > 0) ? (kHeadDim + 2) * 4u : 8u;
+    mbar_arrive_expect_tx(&bar_s, sb);
+  }
   float v[5];
   if (kEmbed) {
     int64_t tok = (pos < p.prompt_len) ? p.prompt[pos] : p.cur[0];
@@ -716,13 +736,19 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     static_assert(S::kProjRows % 8 == 0, "projection rows must fill the 8 warps evenly");
     float acc[kRowsPerWarp];
     dot1280_rows<kRowsPerWarp>(wproj + warp * kHidden, 8 * kHidden, xf, acc);
-    if (lane < kHeadCtas) {  // every lane holds the same sums; lane r stores into cluster rank r
+    if (lane == 0) {
 #pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i)
-        *cluster.map_shared_rank(&qv[rank * S::kProjRows + warp + 8 * i], lane) = __float2half(acc[i] + pbias[i]);
+      for (int i = 0; i < kRowsPerWarp; ++i) qv[rank * S::kProjRows + warp + 8 * i] = __float2half(acc[i] + pbias[i]);
     }
   }
-  cluster.sync();  // q (| k | v) of this head visible in every CTA
+  __syncthreads();
+  if (tid < kHeadCtas && tid != rank) {  // this CTA's rows into the same place of every other CTA
+    const uint4* src = reinterpret_cast<const uint4*>(qv + rank * S::kProjRows);
+    const uint32_t dst = cluster_map(qv + rank * S::kProjRows, tid), rb = cluster_map(&bar_x, tid);
+#pragma unroll
+    for (int c = 0; c < S::kProjRows * 2 / 16; ++c) st_async_v4(dst + 16 * c, src[c], rb);
+  }
+  if (!mbar_wait_cluster(&bar_x, 0)) flag_error(FW_DEVERR_TIMEOUT);  // q (| k | v) of this head complete
   // The next launch is released only now: its weight prefetch (a burst of bulk copies) would
   // otherwise queue in front of this kernel's loads of h, and this kernel runs long enough after
   // this point for that prefetch to complete.
@@ -755,17 +781,26 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
           U[u].q[2 * t + 1] = qf.y;
         }
         unit_sync(1 + u);
-        attn_unit64<kHeadCtas>(ks, vs, n, p.scale, t, U[u], 1 + u, &sm_acc[split][0], &sm_m[split], &sm_l[split]);
+        attn_unit64<kHeadCtas>(ks, vs, n, p.scale, t, U[u], 1 + u, &sm_acc[split][0], &sm_m[split], &sm_l[split],
+                               &bar_s);
       } else if (t == 0) {
+        sm_m[split] = -INFINITY;
+        sm_l[split] = 0.f;
 #pragma unroll
         for (int r = 0; r < kHeadCtas; ++r) {
-          *cluster.map_shared_rank(&sm_m[split], r) = -INFINITY;
-          *cluster.map_shared_rank(&sm_l[split], r) = 0.f;
+          if (r == rank) continue;
+          const uint32_t rb = cluster_map(&bar_s, r);
+          st_async_b32(cluster_map(&sm_m[split], r), __float_as_uint(-INFINITY), rb);
+          st_async_b32(cluster_map(&sm_l[split], r), __float_as_uint(0.f), rb);
         }
       }
     }
   }
-  cluster.sync();  // every split's partial visible in every CTA; no DSMEM access after this point
+  if (!mbar_wait_cluster(&bar_s, 0)) flag_error(FW_DEVERR_TIMEOUT);  // every split's partial received
+  // No CTA exits before all have received their partials (the wait at each exit below), so no st.async
+  // targets a CTA that has exited.
+  cluster_arrive_relaxed();
+  __syncthreads();  // this CTA's own partials (plain stores) visible to all its threads
 
   // ---- 3. split combine (whisper_kernels.cu:193-213 order), in every CTA: the split weights
   // exp(m_s - m) are computed one per thread, then the sums run in split order ----
@@ -827,7 +862,10 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   __syncthreads();
   if (tid == 0) s_last = atomic_add_acq_rel(p.counter + rank, 1u) == static_cast<unsigned>(heads - 1);
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) {
+    cluster_wait();
+    return;
+  }
   if (tid < kOutRows) {
     const int r = row0 + tid;
     float pv[kHeads];
@@ -839,6 +877,7 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     p.h[r] = __float2half(__half2float(hs[r]) + round_half(acc + obias));
   }
   if (tid == 0) p.counter[rank] = 0u;
+  cluster_wait();
 }
 
 // ---------------------------------------------------------------------------------------------
