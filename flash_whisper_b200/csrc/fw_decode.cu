@@ -488,12 +488,12 @@ __global__ void __launch_bounds__(64) attn_split_kernel(AttnParams p) {
   }
 
   if (p.counters == nullptr) return;
-  __threadfence();
+  // thread 0's acq_rel arrival releases this CTA's partial (ordered before it by the barrier) and, in
+  // the last CTA, acquires every other split's
   __syncthreads();
-  if (t == 0) U.last = atomicAdd(p.counters + head, 1u) == static_cast<unsigned>(splits - 1);
+  if (t == 0) U.last = atomic_add_acq_rel(p.counters + head, 1u) == static_cast<unsigned>(splits - 1);
   __syncthreads();
   if (!U.last) return;
-  __threadfence();
   if (t == 0) p.counters[head] = 0u;
   combine_unit64(U, 0, t, p.part_m + head * splits, p.part_l + head * splits,
                  p.part_acc + static_cast<size_t>(head) * splits * kHeadDim, splits, p.out + head * kHeadDim);
@@ -1048,11 +1048,8 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
     unsigned long long m = 0;
     for (int i = 0; i < 8; ++i) m = warp_best[i] > m ? warp_best[i] : m;
     if (m) atomicMax(p.best, m);
-    if (kFinalize) {
-      __threadfence();
-      const unsigned prev = atomicAdd(p.counter, 1u);
-      if (prev == gridDim.x - 1) {
-        __threadfence();
+    if (kFinalize) {  // the acq_rel arrival releases this CTA's maximum and, in the last CTA, acquires all
+      if (atomic_add_acq_rel(p.counter, 1u) == gridDim.x - 1) {
         const unsigned long long b = atomicExch(p.best, 0ull);
         finalize_token(b, p.tokens, p.n_tokens, p.state, p.cur, p.max_pos, p.prompt_len);
         *p.counter = 0u;
@@ -1085,7 +1082,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(LmParams p) {
 // the packed-key maximum of those; the global argmax row is always among its CTA's survivors, so
 // the result equals lm_head_kernel's. If T is not finite or |T| >= 32768 (fp16 overflow makes
 // distant values tie at infinity) every unsuppressed row of the CTA is recomputed.
-constexpr int kQStages = 8;                             // TMA ring depth (16 KB stages)
+constexpr int kQStagesMax = 8;                          // TMA ring depth (16 KB stages), batched head
 constexpr int kQTileRows = 128;                         // MMA M: vocab rows per accumulator tile
 constexpr int kQBoxRows = 32;                           // rows per TMA box
 constexpr int kQChunk = 128;                            // K bytes per stage (one 128-byte swizzle row)
@@ -1161,9 +1158,13 @@ __device__ __forceinline__ void dot1280_ptrs(const half* const (&rows)[kRows], c
 // stage ring.
 template <int kClips>
 struct LmqShape {
+  // The batch-1 head keeps 6 stages so that a CTA (122 KB of shared memory) fits on an SM beside one
+  // of the preceding fc2 launch (103 KB): it then starts, and requests its first stages, while fc2
+  // runs instead of after it.
+  static constexpr int kStages = kClips == 1 ? 6 : kQStagesMax;
   static constexpr int kN = 2 * kClips <= 8 ? 8 : 16;
   static constexpr int kXBytes = kQChunks * kN * kQChunk;
-  static constexpr int kYsOff = kQStages * kQStageBytes + kXBytes;
+  static constexpr int kYsOff = kStages * kQStageBytes + kXBytes;
   static constexpr int kUbOff = kYsOff + kClips * kHidden * 2;
   static constexpr int kCandOff = kUbOff + kClips * kLmMaxRowsPerCta * 4;
   static constexpr int kSmem = kCandOff + kClips * kLmMaxRowsPerCta * 2 + 1024;
@@ -1171,7 +1172,7 @@ struct LmqShape {
 };
 
 // Warp roles: warp 0 streams the CTA's int8 rows (32-row x 128-byte TMA boxes, 128B swizzle) through
-// a kQStages ring, the first stages requested before the PDL wait; warp 1 owns TMEM and issues
+// a kStages ring, the first stages requested before the PDL wait; warp 1 owns TMEM and issues
 // tcgen05.mma kind::i8 (M = 128 rows, N = 8 or 16, K = 32) of each tile against the B operand
 // [x_hi; x_lo] of every clip (xq = 128 x_hi + x_lo, both int8) into one of two TMEM accumulators;
 // warps 2-5 read each row's two int32 sums per clip (tcgen05.ld, TMEM lane = row) and form approx_r
@@ -1182,8 +1183,8 @@ template <bool kLN, bool kFinalize, int kClips>
 __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant__ CUtensorMap tmW, LmParams p) {
   using S = LmqShape<kClips>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kQStages];
-  __shared__ __align__(8) uint64_t empty[kQStages];
+  __shared__ __align__(8) uint64_t full[S::kStages];
+  __shared__ __align__(8) uint64_t empty[S::kStages];
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
@@ -1199,7 +1200,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* stages = smem_raw + (base - raw);
-  uint8_t* xb = stages + kQStages * kQStageBytes;
+  uint8_t* xb = stages + S::kStages * kQStageBytes;
   half* ys = reinterpret_cast<half*>(stages + S::kYsOff);                // [kClips][1280]
   float* ub = reinterpret_cast<float*>(stages + S::kUbOff);              // [kClips][kLmMaxRowsPerCta]
   unsigned short* cand = reinterpret_cast<unsigned short*>(stages + S::kCandOff);
@@ -1211,7 +1212,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   const int n_tiles = (nrows + kQTileRows - 1) / kQTileRows;
   const int total = n_tiles * kQChunks;
   auto issue = [&](int it, uint64_t policy) {
-    const int t = it / kQChunks, c = it - t * kQChunks, s = it % kQStages;
+    const int t = it / kQChunks, c = it - t * kQChunks, s = it % S::kStages;
     const int boxes = (min(kQTileRows, nrows - t * kQTileRows) + kQBoxRows - 1) / kQBoxRows;
     mbar_arrive_expect_tx(&full[s], static_cast<unsigned>(boxes * kQBoxRows * kQChunk));
     for (int b = 0; b < boxes; ++b)
@@ -1220,7 +1221,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   };
 
   if (warp == 0 && lane == 0) {
-    for (int s = 0; s < kQStages; ++s) {
+    for (int s = 0; s < S::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -1231,7 +1232,7 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
     mbar_fence_init();
     tma_prefetch_desc(&tmW);
     const uint64_t policy = policy_evict_first();
-    for (int it = 0; it < kQStages && it < total; ++it) issue(it, policy);  // weights: before the wait
+    for (int it = 0; it < S::kStages && it < total; ++it) issue(it, policy);  // weights: before the wait
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, S::kTmemCols);
@@ -1440,9 +1441,9 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t policy = policy_evict_first();
-      for (int it = kQStages; it < total; ++it) {
-        const int s = it % kQStages;
-        if (!mbar_wait(&empty[s], ((it / kQStages) & 1) ^ 1)) {
+      for (int it = S::kStages; it < total; ++it) {
+        const int s = it % S::kStages;
+        if (!mbar_wait(&empty[s], ((it / S::kStages) & 1) ^ 1)) {
           flag_error(FW_DEVERR_TIMEOUT);
           break;
         }
@@ -1463,8 +1464,8 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(buf * S::kN);
         for (int c = 0; c < kQChunks; ++c) {
-          const int it = t * kQChunks + c, s = it % kQStages;
-          if (!mbar_wait(&full[s], (it / kQStages) & 1)) {
+          const int it = t * kQChunks + c, s = it % S::kStages;
+          if (!mbar_wait(&full[s], (it / S::kStages) & 1)) {
             flag_error(FW_DEVERR_TIMEOUT);
             ok = false;
             break;
@@ -1566,8 +1567,16 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
     }
     const bool all_rows = !(fabsf(t) < 32768.f) || !(bm < 32768.f);
     const float thr = t - (0x1p-9f * (fabsf(t) + 2.f * bm) + 0x1p-23f);
-    for (int i = threadIdx.x; i < nrows; i += 256) {
-      if (!maskc[0][i] && (all_rows || ub[i] >= thr)) cand[atomicAdd(&ncand[0], 1)] = static_cast<unsigned short>(i);
+    // compacted with a ballot: one shared atomic per warp and 32 rows (the rescoring order does not
+    // matter, the packed keys are max-reduced)
+    for (int i0 = warp * 32; i0 < nrows; i0 += 256) {
+      const int i = i0 + lane;
+      const bool take = i < nrows && !maskc[0][i] && (all_rows || ub[i] >= thr);
+      const unsigned bal = __ballot_sync(0xffffffffu, take);
+      int base = 0;
+      if (lane == 0 && bal) base = atomicAdd(&ncand[0], __popc(bal));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (take) cand[base + __popc(bal & ((1u << lane) - 1u))] = static_cast<unsigned short>(i);
     }
   } else if (warp < C) {  // warp w selects clip w's rows, compacted with a ballot (no atomics)
     const int c = warp;
@@ -1633,11 +1642,8 @@ __global__ void __launch_bounds__(256, 1) lm_head_q_kernel(const __grid_constant
       for (int i = 0; i < 8; ++i) m = warp_best[c][i] > m ? warp_best[c][i] : m;
       if (m) atomicMax(p.best + c, m);
     }
-    if (kFinalize) {
-      __threadfence();
-      const unsigned prev = atomicAdd(p.counter, 1u);
-      if (prev == gridDim.x - 1) {
-        __threadfence();
+    if (kFinalize) {  // the acq_rel arrival releases this CTA's maxima and, in the last CTA, acquires all
+      if (atomic_add_acq_rel(p.counter, 1u) == gridDim.x - 1) {
         for (int c = 0; c < C; ++c) {
           const unsigned long long b = atomicExch(p.best + c, 0ull);
           finalize_token(b, p.tokens + c * p.tokens_stride, p.n_tokens, p.state + 2 * c, p.cur + c, p.max_pos,
