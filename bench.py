@@ -43,6 +43,7 @@ import argparse
 import datetime
 import json
 import os
+import select
 import statistics
 import subprocess
 import sys
@@ -95,12 +96,17 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        self.first = None
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
                                           '--format=csv,noheader,nounits', '-lms', '200'],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+        if self.proc is not None:  # nvidia-smi takes a while to start: let it be sampling before timing
+            ready, _, _ = select.select([self.proc.stdout], [], [], 5.0)
+            if ready:
+                self.first = self.proc.stdout.readline()
         return self
 
     def __exit__(self, *exc):
@@ -113,6 +119,8 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        if not self.lines and self.first and self.first.strip():
+            self.lines = [self.first]  # a window shorter than the sampling period: the sample just before it
 
     def summary(self):
         sm, mx, reasons = [], None, set()

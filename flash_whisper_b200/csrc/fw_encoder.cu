@@ -589,9 +589,11 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const half* __restr
 //   warp 1 (one lane): S = Q K^T into TMEM, then O += P V into TMEM, one 64-key block at a time;
 //                      S of block j + 1 is issued as soon as the softmax has read S of block j
 //   warps 2-5: one thread per query row (TMEM lane): online softmax of S (exp2, running max and
-//              sum in fp32), P as fp16 into a 128B-swizzled K-major shared tile (the A operand of
-//              the P V MMA), rescaling of the O row in TMEM when the running max grows, and the
-//              final O / l store.
+//              sum in fp32), P as fp16 into one of two 128B-swizzled K-major shared tiles (the A
+//              operand of the P V MMA), and the final O / l store. The max used for P moves only
+//              when a row's block max exceeds it by more than 2^8 (P <= 256 in fp16), and only then
+//              is the O row in TMEM rescaled; so the softmax of block j waits for P V of block j - 2
+//              (its P buffer), not j - 1, and P V overlaps the next block's softmax.
 // V is read transposed ([heads * 64, seq_pad], keys contiguous) so both MMAs use K-major operands.
 // q arrives pre-scaled by 1/8 (HF WhisperAttention), so S is used unscaled.
 __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -615,14 +617,14 @@ constexpr int kAttnStages = 3;
 constexpr uint32_t kAttnQBytes = kAttnQ * 64 * 2;   // 16 KB
 constexpr uint32_t kAttnKBytes = kAttnK * 64 * 2;   // 8 KB
 constexpr uint32_t kAttnPBytes = kAttnQ * kAttnK * 2;  // 16 KB
-constexpr int kAttnSmem = kAttnQBytes + 2 * kAttnStages * kAttnKBytes + kAttnPBytes + 1024;
+constexpr int kAttnSmem = kAttnQBytes + 2 * kAttnStages * kAttnKBytes + 2 * kAttnPBytes + 1024;
 
 __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQK,
                                                              const __grid_constant__ CUtensorMap tmVt, int kcol,
                                                              half* __restrict__ out, int ldo, int seq) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_q, full_k[kAttnStages], empty_k[kAttnStages], full_v[kAttnStages],
-      empty_v[kAttnStages], s_full, s_free, p_full, o_done;
+      empty_v[kAttnStages], s_full[2], s_free[2], p_full[2], o_done[2];
   __shared__ uint32_t tmem_base_sh;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -644,16 +646,18 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
       mbar_init(&full_v[i], 1);
       mbar_init(&empty_v[i], 1);
     }
-    mbar_init(&s_full, 1);
-    mbar_init(&s_free, 4);
-    mbar_init(&p_full, 4);
-    mbar_init(&o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);  // S buffer i holds the block's scores (block j uses buffer j & 1)
+      mbar_init(&s_free[i], 4);  // the softmax has read S buffer i
+      mbar_init(&p_full[i], 4);  // P buffer i full (block j uses buffer j & 1)
+      mbar_init(&o_done[i], 1);  // P V of the last block that used buffer i complete
+    }
     mbar_fence_init();
     tma_prefetch_desc(&tmQK);
     tma_prefetch_desc(&tmVt);
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_sh, 128);  // S: columns 0-63, O: columns 64-127
+    tmem_alloc(&tmem_base_sh, 256);  // S: columns 0-63 and 64-127 (two blocks), O: columns 128-191
     tmem_relinquish();
   }
   tc_fence_before();
@@ -688,41 +692,46 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(kAttnQ, 64);  // S: N = 64 keys; O: N = 64 dims
-      const uint32_t s_tmem = tmem, o_tmem = tmem + 64;
+      const uint32_t o_tmem = tmem + 128;
       bool ok = mbar_wait(&bar_q, 0);
-      auto issue_s = [&](int j) {  // S = Q K_j^T
+      auto issue_s = [&](int j) {  // S_j = Q K_j^T into S buffer j & 1
         const int st = j % kAttnStages;
         if (!mbar_wait(&full_k[st], (j / kAttnStages) & 1u)) return false;
         tc_fence_after();
         const uint64_t ad = sw128_desc(base), bd = sw128_desc(smem_u32(ks + st * kAttnKBytes));
+        const uint32_t s_tmem = tmem + static_cast<uint32_t>((j & 1) * 64);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) tc_mma_f16(s_tmem, ad + 2 * kk, bd + 2 * kk, idesc, kk != 0 ? 1u : 0u);
         tc_commit(&empty_k[st]);
-        tc_commit(&s_full);
+        tc_commit(&s_full[j & 1]);
         return true;
       };
       if (ok) ok = issue_s(0);
+      if (ok && nkb > 1) ok = issue_s(1);
       for (int j = 0; ok && j < nkb; ++j) {
-        // S_{j+1} may overwrite S as soon as the softmax has read S_j
-        if (!mbar_wait(&s_free, j & 1u)) {
-          ok = false;
-          break;
+        // S_{j+2} reuses S buffer j & 1 once the softmax has read S_j
+        if (j + 2 < nkb) {
+          if (!mbar_wait(&s_free[j & 1], (j >> 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!(ok = issue_s(j + 2))) break;
         }
-        tc_fence_after();
-        if (j + 1 < nkb && !(ok = issue_s(j + 1))) break;
         // O += P_j V_j
         const int st = j % kAttnStages;
-        if (!mbar_wait(&p_full, j & 1u) || !mbar_wait(&full_v[st], (j / kAttnStages) & 1u)) {
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1u) || !mbar_wait(&full_v[st], (j / kAttnStages) & 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t ad = sw128_desc(smem_u32(ps)), bd = sw128_desc(smem_u32(vts + st * kAttnKBytes));
+        const uint64_t ad = sw128_desc(smem_u32(ps + (j & 1) * kAttnPBytes));
+        const uint64_t bd = sw128_desc(smem_u32(vts + st * kAttnKBytes));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           tc_mma_f16(o_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (j | kk) != 0 ? 1u : 0u);
         tc_commit(&empty_v[st]);
-        tc_commit(&o_done);
+        tc_commit(&o_done[j & 1]);
       }
       if (!ok) enc_flag(FW_DEVERR_TIMEOUT);
     }
@@ -731,86 +740,101 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
     const int r = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     constexpr float kLog2e = 1.4426950408889634f;
+    constexpr float kGrow = 8.f;  // log2 units: the max used for P lags the true max by at most this
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
-      if (!mbar_wait_warp(&s_full, j & 1u)) {
+      if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1u)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float sv[64];
+      {
+        uint32_t u[4][16];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[16];
-        tc_ld16(lane_base + c * 16, u);
+        for (int c = 0; c < 4; ++c) tc_ld16(lane_base + (j & 1) * 64 + c * 16, u[c]);
         tc_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sv[c * 16 + i] = __uint_as_float(u[i]) * kLog2e;
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sv[c * 16 + i] = __uint_as_float(u[c][i]);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free);  // S may now be overwritten by the next block's MMA
+      if (lane == 0) mbar_arrive(&s_free[j & 1]);  // S buffer j & 1 may now take block j + 2
       const int kvalid = seq - j * kAttnK;
-      float mb = -INFINITY;
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent max chains
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         if (i >= kvalid) sv[i] = -INFINITY;
-        mb = fmaxf(mb, sv[i]);
+        mq[i & 3] = fmaxf(mq[i & 3], sv[i]);
       }
-      const float m_new = fmaxf(m, mb);
-      const float corr = fast_exp2(m - m_new);  // 0 on the first block (m = -inf)
-      float sum = 0.f;
+      const float mb = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * kLog2e;
+      // The TMEM accesses of a rescale need the whole warp: it happens when any row's max grew by
+      // more than kGrow (always on the first block, where m = -inf); rows whose max did not grow get
+      // corr = 1 exactly.
+      const bool rescale = __any_sync(0xffffffffu, mb > m + kGrow);
+      float corr = 1.f;
+      if (rescale) {
+        const float m_new = fmaxf(m, mb);
+        corr = fast_exp2(m - m_new);  // 0 on the first block
+        m = m_new;
+      }
+      float sq[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
       uint32_t pk[32];
+      const float nm = -m;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = fast_exp2(sv[2 * i] - m_new), p1 = fast_exp2(sv[2 * i + 1] - m_new);
-        sum += p0 + p1;
+        const float p0 = fast_exp2(fmaf(sv[2 * i], kLog2e, nm)), p1 = fast_exp2(fmaf(sv[2 * i + 1], kLog2e, nm));
+        sq[i & 3] += p0 + p1;
         half2 h2 = __floats2half2_rn(p0, p1);
         pk[i] = *reinterpret_cast<uint32_t*>(&h2);
       }
-      l = l * corr + sum;
-      // P and O are free once the previous block's P V MMA has completed
-      if (j > 0) {
-        if (!mbar_wait_warp(&o_done, (j - 1) & 1u)) {
+      l = l * corr + ((sq[0] + sq[1]) + (sq[2] + sq[3]));
+      // P buffer j & 1 is free once P V of block j - 2 has completed
+      if (j >= 2 && !mbar_wait_warp(&o_done[j & 1], ((j >> 1) - 1) & 1u)) {
+        ok = false;
+        break;
+      }
+      if (rescale && j > 0) {  // O holds P V of blocks 0 .. j - 1 once block j - 1's has completed
+        if (!mbar_wait_warp(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // rescale O when the running max of any row of this warp grew (rows whose max did not grow
-        // have corr == 1 exactly); the TMEM accesses need the whole warp
-        if (__any_sync(0xffffffffu, m_new > m)) {
+        uint32_t u[4][16];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t u[16];
-            tc_ld16(lane_base + 64 + c * 16, u);
-            tc_wait_ld();
+        for (int c = 0; c < 4; ++c) tc_ld16(lane_base + 128 + c * 16, u[c]);
+        tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
-            tc_st16(lane_base + 64 + c * 16, u);
-          }
-          tc_wait_st();
-        }
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) u[c][i] = __float_as_uint(__uint_as_float(u[c][i]) * corr);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc_st16(lane_base + 128 + c * 16, u[c]);
+        tc_wait_st();
       }
-      m = m_new;
       // P row r: 8 chunks of 16 bytes, chunk c at r * 128 + ((c ^ (r & 7)) * 16) (128B swizzle)
+      uint8_t* pb = ps + (j & 1) * kAttnPBytes;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(ps + r * 128 + ((c ^ (r & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(pb + r * 128 + ((c ^ (r & 7)) << 4)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       fence_proxy_async_shared();  // generic-proxy P stores -> tensor-core reads
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full);
+      if (lane == 0) mbar_arrive(&p_full[j & 1]);
     }
-    if (ok && nkb > 0 && mbar_wait_warp(&o_done, (nkb - 1) & 1u)) {
+    // the last block's P V completes after every earlier MMA of this CTA
+    if (ok && nkb > 0 && mbar_wait_warp(&o_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1u)) {
       tc_fence_after();
       const float inv = 1.f / l;
       const int row = q0 + r;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t u[16];
-        tc_ld16(lane_base + 64 + c * 16, u);
+        tc_ld16(lane_base + 128 + c * 16, u);
         tc_wait_ld();
         if (row < seq) {
           uint4 w[2];
@@ -831,7 +855,7 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
