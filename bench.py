@@ -68,12 +68,12 @@ CONFIG3 = {'workload': 'BASELINE config 3: GPU log-mel + graphed 32-layer encode
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the ncu captures in profiles/
 # (decode_attention_blocks.txt, decode_fc1_fc2.txt, lm_head_q_decode_step.txt, batched_decode_step.txt)
-NCU_TRAFFIC = {'self_block': 13_180_672, 'cross_block': 14_285_568, 'fc1': 13_154_304, 'fc2': 13_139_712,
-               'lm_head': 77_523_968}
+NCU_TRAFFIC = {'self_block': 13_182_464, 'cross_block': 14_287_360, 'fc1': 13_154_816, 'fc2': 13_139_456,
+               'lm_head': 77_378_304}
 # the batched capture's self attention runs at length 5, not the table's 116: no traffic figure for it
-BATCH_NCU_TRAFFIC = {'qkv': 9_908_480, 'self_attention': None, 'out_proj': 3_346_688, 'cross_q': 3_344_384,
-                     'cross_attention': 61_842_432, 'cross_out_proj': 3_346_944, 'fc1': 13_209_088,
-                     'fc2': 13_238_016, 'lm_head': 77_309_184}
+BATCH_NCU_TRAFFIC = {'qkv': 9_908_480, 'self_attention': None, 'out_proj': 3_346_688, 'cross_q': 3_344_128,
+                     'cross_attention': 61_825_280, 'cross_out_proj': 3_346_688, 'fc1': 13_209_344,
+                     'fc2': 13_238_272, 'lm_head': 77_309_184}
 
 
 def peaks():
