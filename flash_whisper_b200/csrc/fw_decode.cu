@@ -569,6 +569,14 @@ struct HeadBlockParams {
   float* part;            // fp32 [heads, 1280] per-head output-projection partials
   unsigned int* counter;  // [kHeadCtas] arrival counters, zero before, left zero
   half* attn_out;         // optional [heads * 64] attention output (written by rank 0)
+  // Deferred residual. With `defer` the block stops after writing its partials: the next block
+  // (`res_part` set) forms h + fp16(sum of those partials + res_bias) itself, each CTA of a cluster
+  // for its 160-row block, exchanged over DSMEM, instead of this block's last CTAs writing h and the
+  // next launch reading it back. The arithmetic is the same sum in head order.
+  bool defer;
+  const float* res_part;  // [heads, 1280] partials of the previous (deferred) block, or null
+  const half* res_bias;   // [1280] that block's output-projection bias
+  half* h_in_out;         // optional [1280]: the formed residual input, written by head 0's CTAs
 };
 
 template <bool kSelf>
@@ -588,7 +596,7 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   using S = HeadBlockShape<kSelf>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar_w, bar_kv, bar_o;
-  __shared__ __align__(8) uint64_t bar_x, bar_s;  // DSMEM exchanges: projection rows, split partials
+  __shared__ __align__(8) uint64_t bar_x, bar_s, bar_h;  // DSMEM exchanges: rows, split partials, residual
   __shared__ float red[16];
   __shared__ __align__(16) half ys[kHidden];
   __shared__ __align__(16) half hs[kHidden];                   // residual-stream input (for step 5)
@@ -635,8 +643,10 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     mbar_init(&bar_o, 1);
     mbar_init(&bar_x, 1);
     mbar_init(&bar_s, 1);
+    mbar_init(&bar_h, 1);
     mbar_fence_init();
     mbar_arrive_expect_tx(&bar_x, (kHeadCtas - 1) * S::kProjRows * 2);  // the other CTAs' rows
+    if (p.res_part) mbar_arrive_expect_tx(&bar_h, (kHeadCtas - 1) * kOutRows * 2);  // their residual rows
     mbar_arrive_expect_tx(&bar_w, S::kProjBytes);
     for (int r = 0; r < S::kProjRows; ++r)
       bulk_g2s_stream(wproj + r * kHidden, p.w + static_cast<size_t>(proj_row(rank * S::kProjRows + r)) * kHidden,
@@ -717,6 +727,33 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     const half* pr = p.pos_embed + static_cast<size_t>(pos) * kHidden;
 #pragma unroll
     for (int i = 0; i < 5; ++i) v[i] = round_half(__half2float(er[tid + i * 256]) + __half2float(pr[tid + i * 256]));
+  } else if (p.res_part) {
+    // this CTA's 160 rows of h_in = h + fp16(sum over heads, in order, of the previous block's partials
+    // + its bias) — the previous block's last-CTA arithmetic — then the rows to the cluster's other CTAs
+    cluster_wait();  // every CTA of the cluster is running (its mbarriers initialised)
+    if (tid < kOutRows) {
+      const int e = rank * kOutRows + tid;
+      float pv[kHeads];
+#pragma unroll
+      for (int hh = 0; hh < kHeads; ++hh) pv[hh] = __ldcg(p.res_part + static_cast<size_t>(hh) * kHidden + e);
+      const float h0 = __half2float(p.h[e]), rb = __half2float(p.res_bias[e]);
+      float acc = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < kHeads; ++hh) acc += pv[hh];
+      const half hv = __float2half(h0 + round_half(acc + rb));
+      hs[e] = hv;
+      if (p.h_in_out && head == 0) p.h_in_out[e] = hv;
+    }
+    __syncthreads();
+    constexpr int kChunks = kOutRows * 2 / 16;  // 16-byte pieces of the 160-row block
+    if (tid < (kHeadCtas - 1) * kChunks) {
+      const int dst = tid / kChunks + (tid / kChunks >= rank ? 1 : 0), c = tid % kChunks;
+      const uint4 val = reinterpret_cast<const uint4*>(hs + rank * kOutRows)[c];
+      st_async_v4(cluster_map(hs + rank * kOutRows, dst) + 16 * c, val, cluster_map(&bar_h, dst));
+    }
+    if (!mbar_wait_cluster(&bar_h, 0)) flag_error(FW_DEVERR_TIMEOUT);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = __half2float(hs[tid + i * 256]);
   } else {
 #pragma unroll
     for (int i = 0; i < 5; ++i) v[i] = __half2float(p.h[tid + i * 256]);
@@ -732,7 +769,7 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     float xf[40];
     load_x40(ys, xf);
     if (!mbar_wait(&bar_w, 0)) flag_error(FW_DEVERR_TIMEOUT);
-    cluster_wait();
+    if (!p.res_part) cluster_wait();  // (already waited for in the residual exchange)
     static_assert(S::kProjRows % 8 == 0, "projection rows must fill the 8 warps evenly");
     float acc[kRowsPerWarp];
     dot1280_rows<kRowsPerWarp>(wproj + warp * kHidden, 8 * kHidden, xf, acc);
@@ -856,7 +893,13 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     __stcg(p.part + static_cast<size_t>(head) * kHidden + row0 + tid, acc2[0] + acc2[1]);
   }
 
-  // ---- 5. residual update by the last CTA of this row block ----
+  // ---- 5. residual update by the last CTA of this row block (unless the next block does it) ----
+  if (p.defer) {
+    // layer 0 built h from the embedding: the next block reads it from p.h
+    if (kEmbed && head == 0 && tid < kOutRows) p.h[row0 + tid] = hs[row0 + tid];
+    cluster_wait();
+    return;
+  }
   // Thread 0's acq_rel arrival releases the CTA's partial stores (ordered before it by the barrier)
   // and, in the last CTA, acquires every other CTA's; the second barrier extends that to its threads.
   __syncthreads();
@@ -2895,8 +2938,8 @@ static int check_decoder(const fw_decoder_t* d) {
   FW_REQUIRE(self_splits <= kHeadCtas && cross_splits <= kHeadCtas * kHeadMaxUnits, FW_ERR_SHAPE,
              "decoder_step: max_pos must be <= %d and enc_len <= %d", kHeadCtas * kSplitKeys,
              kHeadCtas * kHeadMaxUnits * kSplitKeys);
-  FW_REQUIRE(d->ws_splits * kHeadDim >= kHidden, FW_ERR_SHAPE,
-             "decoder_step: part_acc must hold heads * 1280 floats (ws_splits >= %d)", kHidden / kHeadDim);
+  FW_REQUIRE(d->ws_splits * kHeadDim >= 2 * kHidden, FW_ERR_SHAPE,
+             "decoder_step: part_acc must hold 2 * heads * 1280 floats (ws_splits >= %d)", 2 * kHidden / kHeadDim);
   return FW_OK;
 }
 
@@ -2958,8 +3001,9 @@ static int decoder_launch(const fw_decoder_t* d, int l, int block, cudaStream_t 
     a.scale = d->scale;
     a.wo = static_cast<const half*>(L.out_w);
     a.bo = static_cast<const half*>(L.out_b);
-    a.part = d->part_acc;
+    a.part = d->part_acc;  // left for the cross block, which forms h + this block's output itself
     a.counter = d->counters;
+    a.defer = true;
     a.attn_out = tl ? tl + FW_TRACE_SELF_ATTN : static_cast<half*>(d->attn);
     return l == 0 ? launch_head_block<true, true>(a, d->heads, s, true)
                   : launch_head_block<true, false>(a, d->heads, s, true);
@@ -2981,7 +3025,10 @@ static int decoder_launch(const fw_decoder_t* d, int l, int block, cudaStream_t 
     c.scale = d->scale;
     c.wo = static_cast<const half*>(L.co_w);
     c.bo = static_cast<const half*>(L.co_b);
-    c.part = d->part_acc;
+    c.res_part = d->part_acc;  // the self block's partials, summed here into h + its output
+    c.res_bias = static_cast<const half*>(L.out_b);
+    c.h_in_out = tl ? tl + FW_TRACE_H_SELF : nullptr;
+    c.part = d->part_acc + static_cast<size_t>(d->heads) * kHidden;
     c.counter = d->counters;
     c.attn_out = tl ? tl + FW_TRACE_CROSS_ATTN : nullptr;
     return launch_head_block<false, false>(c, d->heads, s, true);
@@ -3029,7 +3076,9 @@ static int decoder_one_step(const fw_decoder_t* d, cudaStream_t s, half* trace) 
     for (int block = 0; block < 4; ++block) {
       int rc = decoder_launch(d, l, block, s, tl, nullptr);
       if (rc) return rc;
-      if (tl && (rc = snap(tl + kSnapAt[block], block == 2 ? d->ffn : h, block == 2 ? kFfn : kHidden))) return rc;
+      // (the residual after the self block is formed, and traced, by the cross block)
+      if (tl && block > 0 && (rc = snap(tl + kSnapAt[block], block == 2 ? d->ffn : h, block == 2 ? kFfn : kHidden)))
+        return rc;
     }
   }
   return decoder_launch(d, 0, 4, s, nullptr,

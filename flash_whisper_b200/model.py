@@ -112,7 +112,9 @@ class CustomModel:
         self.tokens = torch.zeros(self.max_pos, dtype=torch.long, device=dev)
         self.best = torch.zeros(1, dtype=torch.long, device=dev)
         self.prompt_t = torch.tensor(self.prompt, dtype=torch.long, device=dev)
-        self.splits = -(-max(self.max_pos, self.enc_len) // SPLIT_KEYS)
+        # split-attention workspace; the fused step also keeps two blocks' output-projection partials
+        # (2 * heads * 1280 floats) in part_acc
+        self.splits = max(-(-max(self.max_pos, self.enc_len) // SPLIT_KEYS), 2 * d // self.head_dim)
         self.part_m = torch.empty(self.heads * self.splits, device=dev)
         self.part_l = torch.empty(self.heads * self.splits, device=dev)
         self.part_acc = torch.empty(self.heads * self.splits * self.head_dim, device=dev)

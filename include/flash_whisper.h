@@ -174,8 +174,9 @@ typedef struct {
   void *h, *qkv, *attn, *cq, *ffn;          /* fp16 [1280] residual, -, [1280] attention output of the
                                                last self block (may be NULL), -, [5120] fc1 output */
   float *part_m, *part_l, *part_acc;        /* part_acc: fp32 [heads * ws_splits * 64] scratch (per-head
-                                               output-projection partials); part_m, part_l unused */
-  int64_t ws_splits;                        /* >= 20 (part_acc holds heads * 1280 floats) */
+                                               output-projection partials of the self and the cross
+                                               block); part_m, part_l unused */
+  int64_t ws_splits;                        /* >= 40 (part_acc holds 2 * heads * 1280 floats) */
   unsigned int* counters;                   /* [heads + 1], zero before the first step; left zero */
   int64_t *cur, *state, *tokens, *best;     /* [1], [2] = {position, count}, [n_tokens], [1] (0) */
   int64_t n_tokens;
