@@ -1787,15 +1787,23 @@ struct GemvParams {
   // residual GEMV
   const half* x;
   half* h_res;
+  // deferred residual (ln_gemv_kernel<.., .., true>, a launch in clusters of kHeadCtas): the LayerNorm
+  // input is h + fp16(sum over heads of res_part + res_bias), formed as head_block_kernel does, and
+  // written to h_out by the first cluster
+  const float* res_part;
+  const half* res_bias;
+  half* h_out;
 };
 
 // kRowsPerWarp = rows_per_cta / 8 (1, 3 or 4): warp w owns rows w, w + 8, ...
-template <int kAct, int kRowsPerWarp>
+template <int kAct, int kRowsPerWarp, bool kRes = false>
 __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t bar, bar_h;
   __shared__ float red[16];
   __shared__ __align__(16) half ys[kHidden];
+  __shared__ __align__(16) half hres[kRes ? kHidden : 8];  // the formed LayerNorm input (kRes)
+  const int crank = kRes ? static_cast<int>(blockIdx.x % kHeadCtas) : 0;  // rank in the cluster
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int nr = min(p.rows_per_cta, p.n_out - r0);
@@ -1803,7 +1811,9 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
 
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
+    if (kRes) mbar_init(&bar_h, 1);
     mbar_fence_init();
+    if (kRes) mbar_arrive_expect_tx(&bar_h, (kHeadCtas - 1) * kOutRows * 2);  // the other CTAs' rows
     if (nr > 0) {
       mbar_arrive_expect_tx(&bar, static_cast<unsigned>(nr) * kHidden * 2);
       for (int r = 0; r < nr; ++r)
@@ -1823,14 +1833,46 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
     bias[i] = (p.b && r < nr) ? __half2float(p.b[r0 + r]) : 0.f;
   }
   __syncthreads();
+  if (kRes) cluster_arrive_relaxed();  // completed before the first DSMEM store
   // Released before the wait: the next launch (fc2 in the decode step) reads only weights before its
   // own wait, so it may start its weight copies while the launch before this one still runs.
   pdl_trigger();
   pdl_wait();
 
   float v[5];
+  if constexpr (kRes) {
+    // rows crank*160 .. +159 of h + fp16(sum over heads, in order, of res_part + res_bias), then those
+    // rows to the cluster's other CTAs (head_block_kernel's residual exchange)
+    const int tid = threadIdx.x;
+    cluster_wait();
+    if (tid < kOutRows) {
+      const int e = crank * kOutRows + tid;
+      float pv[kHeads];
 #pragma unroll
-  for (int i = 0; i < 5; ++i) v[i] = __half2float(p.h[threadIdx.x + i * 256]);
+      for (int hh = 0; hh < kHeads; ++hh) pv[hh] = __ldcg(p.res_part + static_cast<size_t>(hh) * kHidden + e);
+      const float h0 = __half2float(p.h[e]), rb = __half2float(p.res_bias[e]);
+      float acc = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < kHeads; ++hh) acc += pv[hh];
+      const half hv = __float2half(h0 + round_half(acc + rb));
+      hres[e] = hv;
+      if (blockIdx.x < kHeadCtas) p.h_out[e] = hv;  // the first cluster materialises it (fc2's residual)
+    }
+    __syncthreads();
+    constexpr int kChunks = kOutRows * 2 / 16;
+    if (tid < (kHeadCtas - 1) * kChunks) {
+      const int dst = tid / kChunks + (tid / kChunks >= crank ? 1 : 0), c = tid % kChunks;
+      const uint4 val = reinterpret_cast<const uint4*>(hres + crank * kOutRows)[c];
+      st_async_v4(cluster_map(hres + crank * kOutRows, dst) + 16 * c, val, cluster_map(&bar_h, dst));
+    }
+    if (!mbar_wait_cluster(&bar_h, 0)) flag_error(FW_DEVERR_TIMEOUT);
+    cluster_arrive_relaxed();  // every CTA has received its rows once all have arrived (the wait at exit)
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = __half2float(hres[tid + i * 256]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) v[i] = __half2float(p.h[threadIdx.x + i * 256]);
+  }
   float mean, inv;
   ln1280_stats(v, red, p.eps, mean, inv);
 #pragma unroll
@@ -1868,6 +1910,7 @@ __global__ void __launch_bounds__(256) ln_gemv_kernel(GemvParams p) {
       }
     }
   }
+  if (kRes) cluster_wait();
 }
 
 // Residual GEMV: h[r] = fp16(h[r] + fp16(W[r] . x + b[r])) for this CTA's kResidRows rows, x of
@@ -2528,6 +2571,18 @@ static int launch_ln_gemv_t(const GemvParams& p, cudaStream_t s, bool pdl) {
   return launch_status(e, "ln_gemv");
 }
 
+// fc1 of the decode step with the deferred residual of the cross block: 32 rows per CTA, clusters of
+// kHeadCtas (the grid, 160 CTAs, is a multiple)
+static int launch_ln_gemv_res(const GemvParams& p, cudaStream_t s) {
+  const int smem = p.rows_per_cta * kHidden * 2;
+  auto kern = ln_gemv_kernel<1, 4, true>;
+  const int grid = (p.n_out + p.rows_per_cta - 1) / p.rows_per_cta;
+  FW_REQUIRE(p.rows_per_cta == 32 && grid % kHeadCtas == 0, FW_ERR_SHAPE, "ln_gemv: deferred residual needs 32 rows per CTA");
+  cudaError_t e = ensure_smem(kern, smem);
+  if (e == cudaSuccess) e = launch_cluster(kern, dim3(grid), dim3(256), smem, s, true, kHeadCtas, p);
+  return launch_status(e, "ln_gemv");
+}
+
 template <int kAct>
 static int launch_ln_gemv(const GemvParams& p, cudaStream_t s, bool pdl) {
   switch (p.rows_per_cta) {
@@ -2926,9 +2981,10 @@ static int check_decoder(const fw_decoder_t* d) {
   FW_REQUIRE(d->n_layers > 0 && d->n_layers <= FW_MAX_LAYERS, FW_ERR_SHAPE, "decoder_step: bad layer count");
   FW_REQUIRE(d->heads * kHeadDim == kHidden, FW_ERR_SHAPE, "decoder_step: heads * 64 must be %d", kHidden);
   FW_REQUIRE(d->max_pos > 0 && d->enc_len > 0 && d->vocab > 0, FW_ERR_SHAPE, "decoder_step: bad sizes");
-  FW_REQUIRE(d->embed && d->pos_embed && d->lm_head && d->final_g && d->final_b && d->h && d->ffn && d->part_acc &&
-                 d->counters && d->cur && d->state && d->tokens && d->best,
+  FW_REQUIRE(d->embed && d->pos_embed && d->lm_head && d->final_g && d->final_b && d->h && d->cq && d->ffn &&
+                 d->part_acc && d->counters && d->cur && d->state && d->tokens && d->best,
              FW_ERR_NULL, "decoder_step: a required pointer is NULL");
+  FW_REQUIRE(aligned16(d->h) && aligned16(d->cq), FW_ERR_ALIGN, "decoder_step: h and cq must be 16-byte aligned");
   FW_REQUIRE(d->prompt_len == 0 || d->prompt != nullptr, FW_ERR_NULL, "decoder_step: prompt is NULL");
   FW_REQUIRE((d->lm_q == nullptr) == (d->lm_rp == nullptr), FW_ERR_NULL, "decoder_step: set both lm_q and lm_rp or neither");
   FW_REQUIRE(d->lm_q == nullptr || (aligned16(d->lm_q) && aligned16(d->lm_rp)), FW_ERR_ALIGN,
@@ -3027,9 +3083,10 @@ static int decoder_launch(const fw_decoder_t* d, int l, int block, cudaStream_t 
     c.bo = static_cast<const half*>(L.co_b);
     c.res_part = d->part_acc;  // the self block's partials, summed here into h + its output
     c.res_bias = static_cast<const half*>(L.out_b);
-    c.h_in_out = tl ? tl + FW_TRACE_H_SELF : nullptr;
-    c.part = d->part_acc + static_cast<size_t>(d->heads) * kHidden;
+    c.h_in_out = static_cast<half*>(d->cq);  // that residual, for fc1
+    c.part = d->part_acc + static_cast<size_t>(d->heads) * kHidden;  // left for fc1
     c.counter = d->counters;
+    c.defer = true;
     c.attn_out = tl ? tl + FW_TRACE_CROSS_ATTN : nullptr;
     return launch_head_block<false, false>(c, d->heads, s, true);
   }
@@ -3042,11 +3099,14 @@ static int decoder_launch(const fw_decoder_t* d, int l, int block, cudaStream_t 
     g.n_out = kFfn;
     g.k = kHidden;
     g.rows_per_cta = kFc1Rows;
-    g.h = h;
+    g.h = static_cast<const half*>(d->cq);  // the residual after the self block, + the cross partials:
+    g.res_part = d->part_acc + static_cast<size_t>(d->heads) * kHidden;
+    g.res_bias = static_cast<const half*>(L.co_b);
+    g.h_out = h;  // the residual after the cross block, fc2's residual input
     g.gamma = static_cast<const half*>(L.ln3_g);
     g.beta = static_cast<const half*>(L.ln3_b);
     g.eps = d->eps;
-    return launch_ln_gemv<1>(g, s, true);
+    return launch_ln_gemv_res(g, s);
   }
   // fc2 + residual
   GemvParams r{};
@@ -3070,15 +3130,18 @@ static int decoder_one_step(const fw_decoder_t* d, cudaStream_t s, half* trace) 
     cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(n) * sizeof(half), cudaMemcpyDeviceToDevice, s);
     return e == cudaSuccess ? FW_OK : set_error(FW_ERR_LAUNCH, "decoder_step_trace: copy: %s", cudaGetErrorString(e));
   };
-  static const int kSnapAt[4] = {FW_TRACE_H_SELF, FW_TRACE_H_CROSS, FW_TRACE_FFN, FW_TRACE_H_FFN};
+  // after the cross block: the residual after the self block (formed by the cross block, in cq); after
+  // fc1: the residual after the cross block (formed by fc1, in h) and the fc1 output; after fc2: h
+  const half* cq = static_cast<const half*>(d->cq);
   for (int l = 0; l < d->n_layers; ++l) {
     half* tl = trace ? trace + static_cast<size_t>(l) * FW_TRACE_LAYER : nullptr;
     for (int block = 0; block < 4; ++block) {
       int rc = decoder_launch(d, l, block, s, tl, nullptr);
       if (rc) return rc;
-      // (the residual after the self block is formed, and traced, by the cross block)
-      if (tl && block > 0 && (rc = snap(tl + kSnapAt[block], block == 2 ? d->ffn : h, block == 2 ? kFfn : kHidden)))
+      if (tl && block == 1 && (rc = snap(tl + FW_TRACE_H_SELF, cq, kHidden))) return rc;
+      if (tl && block == 2 && ((rc = snap(tl + FW_TRACE_H_CROSS, h, kHidden)) || (rc = snap(tl + FW_TRACE_FFN, d->ffn, kFfn))))
         return rc;
+      if (tl && block == 3 && (rc = snap(tl + FW_TRACE_H_FFN, h, kHidden))) return rc;
     }
   }
   return decoder_launch(d, 0, 4, s, nullptr,

@@ -172,7 +172,9 @@ typedef struct {
   const int64_t* prompt;                   /* [prompt_len] forced input ids (may be NULL if 0) */
   fw_decoder_layer_t layers[FW_MAX_LAYERS];
   void *h, *qkv, *attn, *cq, *ffn;          /* fp16 [1280] residual, -, [1280] attention output of the
-                                               last self block (may be NULL), -, [5120] fc1 output */
+                                               last self block (may be NULL), [1280] scratch (the
+                                               residual after each self block), [5120] fc1 output;
+                                               h and cq 16-byte aligned */
   float *part_m, *part_l, *part_acc;        /* part_acc: fp32 [heads * ws_splits * 64] scratch (per-head
                                                output-projection partials of the self and the cross
                                                block); part_m, part_l unused */

@@ -66,8 +66,8 @@ def test_decoder_step_needs_both_pruned_lm_buffers():
     d = _lib.Decoder()
     d.n_layers, d.heads, d.max_pos, d.enc_len, d.vocab = 4, 20, 448, 1500, 51866
     d.ws_splits = 24
-    for name in ('embed', 'pos_embed', 'lm_head', 'final_g', 'final_b', 'h', 'ffn', 'part_acc', 'counters', 'cur',
-                 'state', 'tokens', 'best'):
+    for name in ('embed', 'pos_embed', 'lm_head', 'final_g', 'final_b', 'h', 'cq', 'ffn', 'part_acc', 'counters',
+                 'cur', 'state', 'tokens', 'best'):
         setattr(d, name, 16)
     d.lm_q = 16  # lm_rp left NULL
     assert lib.fw_decoder_step(ctypes.byref(d), 1, None) == 1
