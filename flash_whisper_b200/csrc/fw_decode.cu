@@ -700,6 +700,7 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   __syncthreads();
   cluster_arrive_relaxed();  // completed by the wait before the first DSMEM store: all CTAs are running
   pdl_wait();
+  if (kSelf) pdl_trigger();  // (the cross block releases fc1 later, see below)
 
   // ---- 1. LayerNorm prologue and this CTA's projection rows ----
   if (kEmbed || (kSelf && !p.state_early)) {
@@ -786,10 +787,11 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     for (int c = 0; c < S::kProjRows * 2 / 16; ++c) st_async_v4(dst + 16 * c, src[c], rb);
   }
   if (!mbar_wait_cluster(&bar_x, 0)) flag_error(FW_DEVERR_TIMEOUT);  // q (| k | v) of this head complete
-  // The next launch is released only now: its weight prefetch (a burst of bulk copies) would
-  // otherwise queue in front of this kernel's loads of h, and this kernel runs long enough after
-  // this point for that prefetch to complete.
-  pdl_trigger();
+  // The cross block releases fc1 only now: fc1's weight prefetch (a burst of bulk copies) would
+  // otherwise queue in front of this kernel's loads, and this kernel runs long enough after this point
+  // for that prefetch to complete. (The self block releases the cross block right after its wait:
+  // measured 0.4 us per token faster; the cross block doing the same was 1.7 us slower.)
+  if (!kSelf) pdl_trigger();
 
   // ---- 2. attention splits ----
   {
