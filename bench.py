@@ -68,7 +68,7 @@ CONFIG3 = {'workload': 'BASELINE config 3: GPU log-mel + graphed 32-layer encode
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the ncu captures in profiles/
 # (decode_attention_blocks.txt, decode_fc1_fc2.txt, lm_head_q_decode_step.txt, batched_decode_step.txt)
-NCU_TRAFFIC = {'self_block': 13_182_464, 'cross_block': 14_287_360, 'fc1': 13_154_816, 'fc2': 13_139_456,
+NCU_TRAFFIC = {'self_block': 13_185_024, 'cross_block': 14_395_392, 'fc1': 13_262_080, 'fc2': 13_139_968,
                'lm_head': 77_378_304}
 # the batched capture's self attention runs at length 5, not the table's 116: no traffic figure for it
 BATCH_NCU_TRAFFIC = {'qkv': 9_908_480, 'self_attention': None, 'out_proj': 3_346_688, 'cross_q': 3_344_128,
