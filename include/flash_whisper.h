@@ -196,7 +196,9 @@ int fw_decoder_step(const fw_decoder_t* d, int steps, fw_stream_t stream);
 /* One launch of the decode step in isolation, as fw_decoder_step issues it (programmatic dependent
  * launch included): block 0 = self-attention block of `layer`, 1 = cross-attention block, 2 = LN3 +
  * fc1 + GELU, 3 = fc2 + residual, 4 = LM head (final LN, argmax, token bookkeeping; `layer` ignored).
- * For per-kernel timing and profiling; a full step is blocks 0-3 of every layer, then block 4. No
+ * For per-kernel timing and profiling; a full step is blocks 0-3 of every layer, then block 4. Blocks
+ * 0 and 1 end with their output-projection partials in part_acc: block 1 adds block 0's to h (into
+ * cq) and block 2 adds block 1's (into h), so only the whole sequence updates h as the step does. No
  * reference counterpart (the reference's step is custom/model.py:107-123 as one sequence). */
 int fw_decoder_launch(const fw_decoder_t* d, int layer, int block, fw_stream_t stream);
 
