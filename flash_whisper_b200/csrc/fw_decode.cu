@@ -526,9 +526,11 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
 //   3. the split combine in every CTA (same arithmetic and order as the reference combine);
 //   4. this head's slice of the output projection, W_o[:, head] . o_head, for 1280 / kHeadCtas rows
 //      per CTA, written as fp32 partials [heads, 1280];
-//   5. the residual update: the last of the `heads` CTAs that hold the same row block (atomic
-//      arrival counter per block, nothing spins) sums the per-head partials in head order, adds the
-//      bias and the residual: h[r] = fp16(h[r] + fp16(sum + b[r])).
+//   5. the residual update h[r] = fp16(h[r] + fp16(sum over heads, in head order, of the partials
+//      + b[r])). In the decode step it is deferred (`defer`): the next launch forms it, each CTA of a
+//      cluster for its 160-row block, exchanged over DSMEM (`res_part`); the cross block does that
+//      for the self block, fc1 for the cross block. Without `defer` the last of the `heads` CTAs
+//      that hold the same row block (one acq_rel arrival per block, nothing spins) does it here.
 // Weight rows, the K/V splits and the output-projection slice (head-major [heads, 1280, 64]) are
 // bulk-copied into shared memory before griddepcontrol.wait. The two exchanges inside the cluster
 // (projection rows, split partials) are st.async stores counted on the receiving CTA's mbarrier, so
@@ -541,7 +543,7 @@ constexpr int kSelfProjRows = 3 * kHeadDim / kHeadCtas;   // q, k, v rows per CT
 constexpr int kCrossProjRows = kHeadDim / kHeadCtas;      // q rows per CTA (8)
 
 struct HeadBlockParams {
-  half* h;  // residual stream [1280]: LN input, updated in place by the last CTAs
+  half* h;  // residual stream [1280]: LN input (updated in place by the last CTAs unless `defer`)
   const half* gamma;
   const half* beta;
   float eps;

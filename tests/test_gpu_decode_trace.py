@@ -5,8 +5,9 @@ fw_decoder_step_trace runs one step with the production kernels and launch confi
 every block's output. Each block is checked against the oracle fed the GPU's own input of that
 block, so a mismatch names the kernel:
 
-  * head_block_kernel<self> (LN1, q/k/v, cache write, split attention, out_proj, residual): the
-    attention output and the new residual stream; the K/V row it writes into the cache must equal,
+  * head_block_kernel<self> (LN1, q/k/v, cache write, split attention, out_proj partials; the cross
+    block forms its residual): the attention output and the new residual stream; the K/V row it
+    writes into the cache must equal,
     bit for bit, what the stand-alone fw_ln_gemv computes for the same h (same LayerNorm and dot
     arithmetic), and match the oracle's within tolerance;
   * head_block_kernel<cross>: attention output and residual stream;
