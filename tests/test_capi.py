@@ -74,6 +74,28 @@ def test_decoder_step_needs_both_pruned_lm_buffers():
     assert b'set both lm_q and lm_rp' in lib.fw_last_error_string()
 
 
+def test_decoder_step_needs_residual_scratch_and_two_partial_sets():
+    """The fused step keeps the self and cross blocks' output-projection partials in part_acc (the next
+    launch forms the residual from them) and the residual after each self block in cq."""
+    lib = _lib.lib()
+    d = _lib.Decoder()
+    d.n_layers, d.heads, d.max_pos, d.enc_len, d.vocab = 4, 20, 448, 1500, 51866
+    for name in ('embed', 'pos_embed', 'lm_head', 'final_g', 'final_b', 'h', 'ffn', 'part_acc', 'counters',
+                 'cur', 'state', 'tokens', 'best'):
+        setattr(d, name, 16)
+    d.ws_splits = 40
+    assert lib.fw_decoder_step(ctypes.byref(d), 1, None) == 1  # cq left NULL
+    assert b'required pointer' in lib.fw_last_error_string()
+    d.cq = 16
+    d.ws_splits = 24  # enough for the attention splits, not for two sets of partials
+    assert lib.fw_decoder_step(ctypes.byref(d), 1, None) == 2
+    assert b'2 * heads * 1280' in lib.fw_last_error_string()
+    d.ws_splits = 40
+    d.cq = 18  # misaligned
+    assert lib.fw_decoder_step(ctypes.byref(d), 1, None) == 3
+    assert b'16-byte aligned' in lib.fw_last_error_string()
+
+
 def test_wrapper_checks_mirror_reference_messages():
     ext = Ext()
     h = torch.zeros(1280, dtype=torch.float16)
