@@ -526,11 +526,11 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
 //   3. the split combine in every CTA (same arithmetic and order as the reference combine);
 //   4. this head's slice of the output projection, W_o[:, head] . o_head, for 1280 / kHeadCtas rows
 //      per CTA, written as fp32 partials [heads, 1280];
-//   5. the residual update h[r] = fp16(h[r] + fp16(sum over heads, in head order, of the partials
-//      + b[r])). In the decode step it is deferred (`defer`): the next launch forms it, each CTA of a
-//      cluster for its 160-row block, exchanged over DSMEM (`res_part`); the cross block does that
-//      for the self block, fc1 for the cross block. Without `defer` the last of the `heads` CTAs
-//      that hold the same row block (one acq_rel arrival per block, nothing spins) does it here.
+// and leaves the residual update h[r] = fp16(h[r] + fp16(sum over heads, in head order, of the
+// partials + b[r])) to the next launch, which forms it itself, each CTA of a cluster for its 160-row
+// block, exchanged over DSMEM (`res_part`): the cross block for the self block, fc1
+// (ln_gemv_kernel<.., .., true>) for the cross block. So no block needs an arrival counter, a
+// last-CTA stage or a write of h that the next launch reads back.
 // Weight rows, the K/V splits and the output-projection slice (head-major [heads, 1280, 64]) are
 // bulk-copied into shared memory before griddepcontrol.wait. The two exchanges inside the cluster
 // (projection rows, split partials) are st.async stores counted on the receiving CTA's mbarrier, so
@@ -543,7 +543,7 @@ constexpr int kSelfProjRows = 3 * kHeadDim / kHeadCtas;   // q, k, v rows per CT
 constexpr int kCrossProjRows = kHeadDim / kHeadCtas;      // q rows per CTA (8)
 
 struct HeadBlockParams {
-  half* h;  // residual stream [1280]: LN input (updated in place by the last CTAs unless `defer`)
+  half* h;  // residual stream [1280]: LN input (layer 0's self block writes the embedded row here)
   const half* gamma;
   const half* beta;
   float eps;
@@ -565,18 +565,13 @@ struct HeadBlockParams {
   half* v;
   int kv_len;
   float scale;
-  // output projection, head-major [heads, 1280, 64], and its bias [1280]
+  // output projection, head-major [heads, 1280, 64] (its bias is added by the next launch)
   const half* wo;
-  const half* bo;
   float* part;            // fp32 [heads, 1280] per-head output-projection partials
-  unsigned int* counter;  // [kHeadCtas] arrival counters, zero before, left zero
   half* attn_out;         // optional [heads * 64] attention output (written by rank 0)
-  // Deferred residual. With `defer` the block stops after writing its partials: the next block
-  // (`res_part` set) forms h + fp16(sum of those partials + res_bias) itself, each CTA of a cluster
-  // for its 160-row block, exchanged over DSMEM, instead of this block's last CTAs writing h and the
-  // next launch reading it back. The arithmetic is the same sum in head order.
-  bool defer;
-  const float* res_part;  // [heads, 1280] partials of the previous (deferred) block, or null
+  // The residual of the previous attention block (cross block only): the LayerNorm input is
+  // h + fp16(sum over heads of res_part + res_bias), formed here.
+  const float* res_part;  // [heads, 1280] partials of the previous block, or null
   const half* res_bias;   // [1280] that block's output-projection bias
   half* h_in_out;         // optional [1280]: the formed residual input, written by head 0's CTAs
 };
@@ -601,7 +596,7 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   __shared__ __align__(8) uint64_t bar_x, bar_s, bar_h;  // DSMEM exchanges: rows, split partials, residual
   __shared__ float red[16];
   __shared__ __align__(16) half ys[kHidden];
-  __shared__ __align__(16) half hs[kHidden];                   // residual-stream input (for step 5)
+  __shared__ __align__(16) half hs[kHidden];                   // residual-stream input
   __shared__ __align__(16) half qv[S::kProjRows * kHeadCtas];  // this head's q (| k | v)
   __shared__ __align__(16) float os[kHeadDim];                  // this head's attention output
   __shared__ __align__(16) SplitScratch U[S::kUnits];
@@ -609,11 +604,9 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
   __shared__ float sm_l[S::kSlots];
   __shared__ __align__(16) float sm_acc[S::kSlots][kHeadDim];
   __shared__ float sm_w[S::kSlots];
-  __shared__ int s_last;
 
   const int rank = blockIdx.x;  // cluster dims (kHeadCtas, 1, 1) over grid (kHeadCtas, heads)
   const int head = blockIdx.y;
-  const int heads = gridDim.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   half* wproj = reinterpret_cast<half*>(smem);
   half* kvs = reinterpret_cast<half*>(smem + S::kProjBytes);
@@ -698,7 +691,6 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     const int r = warp + 8 * i;
     pbias[i] = (p.b && r < S::kProjRows) ? __half2float(p.b[proj_row(rank * S::kProjRows + r)]) : 0.f;
   }
-  const float obias = (p.bo && tid < kOutRows) ? __half2float(p.bo[rank * kOutRows + tid]) : 0.f;
   __syncthreads();
   cluster_arrive_relaxed();  // completed by the wait before the first DSMEM store: all CTAs are running
   pdl_wait();
@@ -897,34 +889,10 @@ __global__ void __launch_bounds__(256, 2) head_block_kernel(HeadBlockParams p) {
     __stcg(p.part + static_cast<size_t>(head) * kHidden + row0 + tid, acc2[0] + acc2[1]);
   }
 
-  // ---- 5. residual update by the last CTA of this row block (unless the next block does it) ----
-  if (p.defer) {
-    // layer 0 built h from the embedding: the next block reads it from p.h
-    if (kEmbed && head == 0 && tid < kOutRows) p.h[row0 + tid] = hs[row0 + tid];
-    cluster_wait();
-    return;
-  }
-  // Thread 0's acq_rel arrival releases the CTA's partial stores (ordered before it by the barrier)
-  // and, in the last CTA, acquires every other CTA's; the second barrier extends that to its threads.
-  __syncthreads();
-  if (tid == 0) s_last = atomic_add_acq_rel(p.counter + rank, 1u) == static_cast<unsigned>(heads - 1);
-  __syncthreads();
-  if (!s_last) {
-    cluster_wait();
-    return;
-  }
-  if (tid < kOutRows) {
-    const int r = row0 + tid;
-    float pv[kHeads];
-#pragma unroll
-    for (int hh = 0; hh < kHeads; ++hh) pv[hh] = __ldcg(p.part + static_cast<size_t>(hh) * kHidden + r);
-    float acc = 0.f;
-#pragma unroll
-    for (int hh = 0; hh < kHeads; ++hh) acc += pv[hh];
-    p.h[r] = __float2half(__half2float(hs[r]) + round_half(acc + obias));
-  }
-  if (tid == 0) p.counter[rank] = 0u;
-  cluster_wait();
+  // ---- 5. the residual is formed by the next launch; layer 0 built h from the embedding, which the
+  // next block reads from p.h ----
+  if (kEmbed && head == 0 && tid < kOutRows) p.h[row0 + tid] = hs[row0 + tid];
+  cluster_wait();  // no CTA exits while a peer may still send it exchange bytes
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -3060,10 +3028,7 @@ static int decoder_launch(const fw_decoder_t* d, int l, int block, cudaStream_t 
     a.kv_len = d->max_pos;
     a.scale = d->scale;
     a.wo = static_cast<const half*>(L.out_w);
-    a.bo = static_cast<const half*>(L.out_b);
     a.part = d->part_acc;  // left for the cross block, which forms h + this block's output itself
-    a.counter = d->counters;
-    a.defer = true;
     a.attn_out = tl ? tl + FW_TRACE_SELF_ATTN : static_cast<half*>(d->attn);
     return l == 0 ? launch_head_block<true, true>(a, d->heads, s, true)
                   : launch_head_block<true, false>(a, d->heads, s, true);
@@ -3083,14 +3048,11 @@ static int decoder_launch(const fw_decoder_t* d, int l, int block, cudaStream_t 
     c.v = const_cast<half*>(static_cast<const half*>(L.cross_v));
     c.kv_len = d->enc_len;
     c.scale = d->scale;
-    c.wo = static_cast<const half*>(L.co_w);
-    c.bo = static_cast<const half*>(L.co_b);
+    c.wo = static_cast<const half*>(L.co_w);  // (its bias co_b is added by fc1)
     c.res_part = d->part_acc;  // the self block's partials, summed here into h + its output
     c.res_bias = static_cast<const half*>(L.out_b);
     c.h_in_out = static_cast<half*>(d->cq);  // that residual, for fc1
     c.part = d->part_acc + static_cast<size_t>(d->heads) * kHidden;  // left for fc1
-    c.counter = d->counters;
-    c.defer = true;
     c.attn_out = tl ? tl + FW_TRACE_CROSS_ATTN : nullptr;
     return launch_head_block<false, false>(c, d->heads, s, true);
   }
