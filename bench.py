@@ -324,12 +324,12 @@ def decode_kernel_table(model, dims, pk, length=116):
     nb = block_bytes(dims, length, pruned)
     per_step = {'self_block': dims.decoder_layers, 'cross_block': dims.decoder_layers, 'fc1': dims.decoder_layers,
                 'fc2': dims.decoder_layers, 'lm_head': 1}
-    names = {'self_block': 'head_block_kernel<self> (LN1 + q/k/v + split attention + cache write + out_proj + '
-                           'residual, 20 clusters x 8 CTAs)',
-             'cross_block': 'head_block_kernel<cross> (LN2 + cross q + split attention over 1500 keys + out_proj '
-                            '+ residual, 20 clusters x 8 CTAs)',
-             'fc1': 'ln_gemv_kernel (LN3 + fc1 5120x1280 + GELU)', 'fc2': 'gemv_residual_kernel (fc2 1280x5120 + '
-                                                                        'residual)',
+    names = {'self_block': 'head_block_kernel<self> (LN1 + q/k/v + split attention + cache write + out_proj '
+                           'partials, 20 clusters x 8 CTAs; its residual is formed by the cross block)',
+             'cross_block': 'head_block_kernel<cross> (self-block residual + LN2 + cross q + split attention over '
+                            '1500 keys + out_proj partials, 20 clusters x 8 CTAs)',
+             'fc1': 'ln_gemv_kernel (cross-block residual + LN3 + fc1 5120x1280 + GELU, clusters of 8)',
+             'fc2': 'gemv_residual_kernel (fc2 1280x5120 + residual)',
              'lm_head': ('lm_head_q_kernel (final LN + int8 tcgen05 GEMV over 51866 rows + exact fp16 rescoring + '
                          'argmax + finalize)' if pruned else 'lm_head_kernel (final LN + fp16 GEMV + argmax)')}
     blocks = {'self_block': (1, 0), 'cross_block': (1, 1), 'fc1': (1, 2), 'fc2': (1, 3), 'lm_head': (0, 4)}
