@@ -18,7 +18,7 @@
 //    t0..t0+127 (input rows stride*t + j) as one box, so no im2col buffer is materialised.
 //  * enc_attn_tc_kernel: bidirectional attention, 128 queries x one head per CTA, online softmax
 //    over 64-key blocks; S = QK^T and O += PV^T on tcgen05 with S and O in TMEM, Q / K / V^T tiles
-//    staged by TMA, one thread per query row for the softmax.
+//    staged by TMA, two threads per query row for the softmax.
 #include <cooperative_groups.h>
 #include <cuda.h>
 
@@ -588,12 +588,17 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const half* __restr
 //   warp 0 (one lane): TMA loads - Q once, then K and V^T blocks through a kAttnStages ring
 //   warp 1 (one lane): S = Q K^T into TMEM, then O += P V into TMEM, one 64-key block at a time;
 //                      S of block j + 1 is issued as soon as the softmax has read S of block j
-//   warps 2-5: one thread per query row (TMEM lane): online softmax of S (exp2, running max and
-//              sum in fp32), P as fp16 into one of two 128B-swizzled K-major shared tiles (the A
-//              operand of the P V MMA), and the final O / l store. The max used for P moves only
-//              when a row's block max exceeds it by more than 2^8 (P <= 256 in fp16), and only then
-//              is the O row in TMEM rescaled; so the softmax of block j waits for P V of block j - 2
-//              (its P buffer), not j - 1, and P V overlaps the next block's softmax.
+//   warps 2-9: two threads per query row (TMEM lane), warp w taking keys 32 ((w - 2) / 4) .. + 31
+//              of each block for the rows of TMEM lane quadrant w % 4: online softmax of S (exp2,
+//              running max and sum in fp32), P as fp16 into one of two 128B-swizzled K-major shared
+//              tiles (the A operand of the P V MMA), and the final O / l store (each warp 32 of the
+//              64 output columns). Both threads of a row take the max over all 64 scores of the
+//              block (the same value, so the same rescale decisions without an exchange); each
+//              sums its own keys and the two sums are added once at the end. The max used for P
+//              moves only when a row's block max exceeds it by more than 2^8 (P <= 256 in fp16),
+//              and only then is the O row in TMEM rescaled; so the softmax of block j waits for
+//              P V of block j - 2 (its P buffer), not j - 1, and P V overlaps the next block's
+//              softmax.
 // V is read transposed ([heads * 64, seq_pad], keys contiguous) so both MMAs use K-major operands.
 // q arrives pre-scaled by 1/8 (HF WhisperAttention), so S is used unscaled.
 __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -618,13 +623,17 @@ constexpr uint32_t kAttnQBytes = kAttnQ * 64 * 2;   // 16 KB
 constexpr uint32_t kAttnKBytes = kAttnK * 64 * 2;   // 8 KB
 constexpr uint32_t kAttnPBytes = kAttnQ * kAttnK * 2;  // 16 KB
 constexpr int kAttnSmem = kAttnQBytes + 2 * kAttnStages * kAttnKBytes + 2 * kAttnPBytes + 1024;
+constexpr int kAttnSoftWarps = 8;  // two per TMEM lane quadrant, each half of a block's keys
+constexpr int kAttnThreads = 32 * (2 + kAttnSoftWarps);
 
-__global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQK,
-                                                             const __grid_constant__ CUtensorMap tmVt, int kcol,
-                                                             half* __restrict__ out, int ldo, int seq) {
+__global__ void __launch_bounds__(kAttnThreads, 2) enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQK,
+                                                                      const __grid_constant__ CUtensorMap tmVt,
+                                                                      int kcol, half* __restrict__ out, int ldo,
+                                                                      int seq) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_q, full_k[kAttnStages], empty_k[kAttnStages], full_v[kAttnStages],
-      empty_v[kAttnStages], s_full[2], s_free[2], p_full[2], o_done[2];
+      empty_v[kAttnStages], s_full[2], s_free[2], p_full[2], o_done[2], l_bar;
+  __shared__ float s_l[2][kAttnQ];  // each row's two partial sums (key halves 0 and 1)
   __shared__ uint32_t tmem_base_sh;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -647,11 +656,12 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
       mbar_init(&empty_v[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);  // S buffer i holds the block's scores (block j uses buffer j & 1)
-      mbar_init(&s_free[i], 4);  // the softmax has read S buffer i
-      mbar_init(&p_full[i], 4);  // P buffer i full (block j uses buffer j & 1)
-      mbar_init(&o_done[i], 1);  // P V of the last block that used buffer i complete
+      mbar_init(&s_full[i], 1);                // S buffer i holds the block's scores (block j uses buffer j & 1)
+      mbar_init(&s_free[i], kAttnSoftWarps);   // the softmax has read S buffer i
+      mbar_init(&p_full[i], kAttnSoftWarps);   // P buffer i full (block j uses buffer j & 1)
+      mbar_init(&o_done[i], 1);                // P V of the last block that used buffer i complete
     }
+    mbar_init(&l_bar, 32 * kAttnSoftWarps);  // every softmax thread has stored its partial sum
     mbar_fence_init();
     tma_prefetch_desc(&tmQK);
     tma_prefetch_desc(&tmVt);
@@ -736,7 +746,8 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
       if (!ok) enc_flag(FW_DEVERR_TIMEOUT);
     }
   } else {
-    const int q = warp & 3;  // TMEM lanes 32q..32q+31
+    const int q = warp & 3;            // TMEM lanes 32q..32q+31
+    const int hs = (warp - 2) >> 2;    // this warp's keys 32 hs .. 32 hs + 31 of each block
     const int r = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     constexpr float kLog2e = 1.4426950408889634f;
@@ -749,26 +760,41 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
         break;
       }
       tc_fence_after();
-      float sv[64];
+      float sv[32], so[32];  // this warp's keys, the other half's keys (only for the row max)
       {
+        const uint32_t sb = lane_base + (j & 1) * 64;
         uint32_t u[4][16];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tc_ld16(lane_base + (j & 1) * 64 + c * 16, u[c]);
+        tc_ld16(sb + hs * 32, u[0]);
+        tc_ld16(sb + hs * 32 + 16, u[1]);
+        tc_ld16(sb + (hs ^ 1) * 32, u[2]);
+        tc_ld16(sb + (hs ^ 1) * 32 + 16, u[3]);
         tc_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 16; ++i) sv[c * 16 + i] = __uint_as_float(u[c][i]);
+        for (int i = 0; i < 16; ++i) {
+          sv[i] = __uint_as_float(u[0][i]);
+          sv[16 + i] = __uint_as_float(u[1][i]);
+          so[i] = __uint_as_float(u[2][i]);
+          so[16 + i] = __uint_as_float(u[3][i]);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[j & 1]);  // S buffer j & 1 may now take block j + 2
       const int kvalid = seq - j * kAttnK;
-      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent max chains
+      if (kvalid < kAttnK) {  // the ragged last block (the same for every thread of the CTA)
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        if (i >= kvalid) sv[i] = -INFINITY;
+        for (int i = 0; i < 32; ++i) {
+          if (hs * 32 + i >= kvalid) sv[i] = -INFINITY;
+          if ((hs ^ 1) * 32 + i >= kvalid) so[i] = -INFINITY;
+        }
+      }
+      // Row max over all 64 keys, four independent chains; fmax is exact, so both warps of a row
+      // get the same value whichever half they hold.
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
         mq[i & 3] = fmaxf(mq[i & 3], sv[i]);
+        mq[(i + 2) & 3] = fmaxf(mq[(i + 2) & 3], so[i]);
       }
       const float mb = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * kLog2e;
       // The TMEM accesses of a rescale need the whole warp: it happens when any row's max grew by
@@ -782,10 +808,10 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
         m = m_new;
       }
       float sq[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
-      uint32_t pk[32];
+      uint32_t pk[16];
       const float nm = -m;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float p0 = fast_exp2(fmaf(sv[2 * i], kLog2e, nm)), p1 = fast_exp2(fmaf(sv[2 * i + 1], kLog2e, nm));
         sq[i & 3] += p0 + p1;
         half2 h2 = __floats2half2_rn(p0, p1);
@@ -803,38 +829,44 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
           break;
         }
         tc_fence_after();
-        uint32_t u[4][16];
+        uint32_t u[2][16];  // this warp's 32 of the 64 O columns
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tc_ld16(lane_base + 128 + c * 16, u[c]);
+        for (int c = 0; c < 2; ++c) tc_ld16(lane_base + 128 + hs * 32 + c * 16, u[c]);
         tc_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int i = 0; i < 16; ++i) u[c][i] = __float_as_uint(__uint_as_float(u[c][i]) * corr);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tc_st16(lane_base + 128 + c * 16, u[c]);
+        for (int c = 0; c < 2; ++c) tc_st16(lane_base + 128 + hs * 32 + c * 16, u[c]);
         tc_wait_st();
       }
-      // P row r: 8 chunks of 16 bytes, chunk c at r * 128 + ((c ^ (r & 7)) * 16) (128B swizzle)
+      // P row r: 8 chunks of 16 bytes, chunk c at r * 128 + ((c ^ (r & 7)) * 16) (128B swizzle);
+      // this warp writes chunks 4 hs .. 4 hs + 3 (its 32 keys)
       uint8_t* pb = ps + (j & 1) * kAttnPBytes;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(pb + r * 128 + ((c ^ (r & 7)) << 4)) =
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(pb + r * 128 + (((hs * 4 + c) ^ (r & 7)) << 4)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       fence_proxy_async_shared();  // generic-proxy P stores -> tensor-core reads
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[j & 1]);
     }
+    // Row sum = the two halves' partial sums (every softmax thread stores and arrives exactly once,
+    // also after a timed-out wait, so the bounded wait below only fails if a warp never got here).
+    s_l[hs][r] = l;
+    mbar_arrive(&l_bar);
     // the last block's P V completes after every earlier MMA of this CTA
-    if (ok && nkb > 0 && mbar_wait_warp(&o_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1u)) {
+    if (ok && nkb > 0 && mbar_wait_warp(&o_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1u) &&
+        mbar_wait_warp(&l_bar, 0)) {
       tc_fence_after();
-      const float inv = 1.f / l;
+      const float inv = 1.f / (s_l[0][r] + s_l[1][r]);
       const int row = q0 + r;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t u[16];
-        tc_ld16(lane_base + 128 + c * 16, u);
+        tc_ld16(lane_base + 128 + hs * 32 + c * 16, u);
         tc_wait_ld();
         if (row < seq) {
           uint4 w[2];
@@ -842,7 +874,7 @@ __global__ void __launch_bounds__(192, 2) enc_attn_tc_kernel(const __grid_consta
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             h[i] = __floats2half2_rn(__uint_as_float(u[2 * i]) * inv, __uint_as_float(u[2 * i + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ldo + head * 64 + c * 16);
+          uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ldo + head * 64 + hs * 32 + c * 16);
           dst[0] = w[0];
           dst[1] = w[1];
         }
@@ -1080,8 +1112,8 @@ static int run_attention(const void* qkv, int64_t ld, int kcol, const void* vt, 
   if (rc) return rc;
   cudaError_t e = ensure_smem(enc_attn_tc_kernel, kAttnSmem);
   if (e == cudaSuccess)
-    e = launch(enc_attn_tc_kernel, dim3((seq + kAttnQ - 1) / kAttnQ, heads), dim3(192), kAttnSmem, s, pdl, tqk, tvt,
-               kcol, static_cast<half*>(out), heads * 64, seq);
+    e = launch(enc_attn_tc_kernel, dim3((seq + kAttnQ - 1) / kAttnQ, heads), dim3(kAttnThreads), kAttnSmem, s, pdl,
+               tqk, tvt, kcol, static_cast<half*>(out), heads * 64, seq);
   return launch_status(e, "encoder_attention");
 }
 
