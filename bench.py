@@ -85,7 +85,8 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi SM clock / throttle-reason sampling during the timed region."""
+    """nvidia-smi SM clock / throttle-reason sampling during the timed region (every 50 ms, so that
+    the ~0.3 s config-3 region gets several samples)."""
 
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
@@ -99,7 +100,7 @@ class ClockSampler:
         self.first = None
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
-                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                          '--format=csv,noheader,nounits', '-lms', '50'],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -439,7 +440,7 @@ def micro_table(model, dims, pk):
     return out
 
 
-def config4(args, model, dims, ranks, rank, world, pk):
+def config4(args, model, dims, ranks, rank, world, local_rank, pk):
     """the 256-clip stream, statically partitioned over the ranks, as batch-1
     streams (one clip at a time through the graphed pipeline). Device time with the audio resident,
     and end to end through transcribe() from host audio."""
@@ -458,12 +459,13 @@ def config4(args, model, dims, ranks, rank, world, pk):
     torch.cuda.synchronize()
     ranks.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for j, i in enumerate(mine):
-        model.wave.copy_(waves[j])
-        model.decode_device(clips[i][2])
-    e1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for j, i in enumerate(mine):
+            model.wave.copy_(waves[j])
+            model.decode_device(clips[i][2])
+        e1.record(stream)
+        torch.cuda.synchronize()
     ranks.barrier()
     dev_ms = e0.elapsed_time(e1)
     max_ms, min_ms = ranks.reduce(dev_ms, 'max'), ranks.reduce(dev_ms, 'min')
@@ -492,10 +494,11 @@ def config4(args, model, dims, ranks, rank, world, pk):
     run_batched()  # warm-up (captures the encoder and chunk graphs)
     torch.cuda.synchronize()
     ranks.barrier()
-    e0.record(stream)
-    run_batched()
-    e1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as b_clocks:
+        e0.record(stream)
+        run_batched()
+        e1.record(stream)
+        torch.cuda.synchronize()
     ranks.barrier()
     b_ms = e0.elapsed_time(e1)
     b_max, b_min = ranks.reduce(b_ms, 'max'), ranks.reduce(b_ms, 'min')
@@ -521,6 +524,7 @@ def config4(args, model, dims, ranks, rank, world, pk):
         'max_rank_ms': round(b_max, 3), 'min_rank_ms': round(b_min, 3),
         'tail_imbalance': round(b_max / b_min - 1.0, 4) if b_min > 0 else None,
         'groups_rank0': len(groups), 'decode_steps_rank0': steps, 'gpu_launches_rank0': b_launches,
+        'clocks': b_clocks.summary(),
     }
     return {
         'workload': f'BASELINE config 4: {len(clips)} clips (seeds 0..{len(clips) - 1}, U[5,30] s from '
@@ -533,6 +537,7 @@ def config4(args, model, dims, ranks, rank, world, pk):
         'tail_imbalance': round(max_ms / min_ms - 1.0, 4) if min_ms > 0 else None,
         'rank_token_loads': {'max': max(loads), 'min': min(loads)},
         'gpu_launches_rank0': launches,
+        'clocks': clocks.summary(),
         'batched': batched,
     }
 
@@ -628,7 +633,7 @@ def bench_ours(args, rank, world, local_rank):
     kernels = decode_kernel_table(model, dims, pk)
     dominant = max(kernels, key=lambda k: kernels[k]['share'])
     micro = micro_table(model, dims, pk) if rank == 0 and not args.lean else None
-    c4 = config4(args, model, dims, ranks, rank, world, pk) if not args.lean else None
+    c4 = config4(args, model, dims, ranks, rank, world, local_rank, pk) if not args.lean else None
 
     avg_len = 4 + N_TOKENS // 2
     pruned = model.lm_q is not None
