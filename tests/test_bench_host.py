@@ -1,5 +1,6 @@
 """CPU tests of bench.py's host logic: the BASELINE config 4 clip set, its static longest-first
-partition over ranks, and the multi-rank reduction bench.py performs, on two gloo ranks."""
+partition over ranks, the clock record parsed from nvidia-smi's CSV samples, and the multi-rank
+reduction bench.py performs, on two gloo ranks."""
 
 import os
 import socket
@@ -26,6 +27,22 @@ def test_clip_set_is_config4():
     assert secs.min() >= 5.0 and secs.max() <= 30.0
     assert all(c[2] == int(round(7.5 * c[1])) for c in clips)
     assert clips == bench.clip_set()  # seeded
+
+
+def test_clock_summary_parses_samples_and_reasons():
+    """The clock record of a timed region: median SM clock under load, the max clock, and every throttle
+    reason seen Active in any sample (fields as bench.ClockSampler.FIELDS asks nvidia-smi for them)."""
+    cs = bench.ClockSampler(0)
+    cs.lines = ['0, 1965, 1965, 612.3, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active',
+                '0, 1950, 1965, 998.1, 0x0000000000000004, Not Active, Not Active, Not Active, Active',
+                '0, 1965, 1965, 640.0, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active',
+                'garbage line']
+    s = cs.summary()
+    assert s == {'sm_mhz': 1965.0, 'sm_max_mhz': 1965.0, 'reasons': ['sw_power_cap'], 'samples': 3}
+    cs.lines = ['0, 1200, 1965, 700.0, 0x0000000000000008, Active, Not Active, Active, Not Active']
+    assert cs.summary()['reasons'] == ['hw_slowdown', 'sw_thermal_slowdown']
+    cs.lines = []
+    assert cs.summary() == {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unavailable']}
 
 
 @pytest.mark.parametrize('world', [1, 2, 3, 4, 8])
