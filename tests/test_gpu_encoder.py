@@ -112,7 +112,7 @@ def test_layernorm_rows_vs_torch(ext):
     _close(y, F.layer_norm(x.float(), (1280,), g.float(), b.float(), 1e-5).half())
 
 
-@pytest.mark.parametrize('seq', [1500, 200, 77])
+@pytest.mark.parametrize('seq', [1500, 200, 77, 33, 20, 1])
 def test_encoder_attention_vs_torch(ext, seq):
     heads = 20
     qkv = _rand(seq, 3 * 1280, seed=seq)
