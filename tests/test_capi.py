@@ -20,6 +20,36 @@ def test_library_exports_every_declared_symbol():
     assert lib.fw_version() == 1
 
 
+def _c_class(decl):
+    """Argument class of one C parameter declaration: pointer, i32, i64 or f32."""
+    decl = decl.strip()
+    if '*' in decl or decl.startswith('fw_stream_t'):
+        return 'ptr'
+    base = decl.rsplit(None, 1)[0] if ' ' in decl else decl
+    return {'int': 'i32', 'int64_t': 'i64', 'float': 'f32'}[base.replace('const ', '').strip()]
+
+
+def _ctypes_class(t):
+    if t in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(t, ctypes._Pointer):
+        return 'ptr'
+    return {ctypes.c_int: 'i32', ctypes.c_int64: 'i64', ctypes.c_float: 'f32'}[t]
+
+
+def test_ctypes_signatures_match_header_prototypes():
+    """Every prototype in include/flash_whisper.h against the ctypes binding: same return type and the
+    same number and kind of arguments (a wrong count or an int passed as int64 would otherwise show up
+    only as wrong results on a GPU)."""
+    import re
+    text = re.sub(r'/\*.*?\*/', '', _lib.HEADER.read_text(), flags=re.S)
+    protos = re.findall(r'^(const char\*|int)\s+(fw_\w+)\((.*?)\);', text, flags=re.M | re.S)
+    assert len(protos) == len(_lib._SIGNATURES)
+    for ret, name, args in protos:
+        res, argtypes = _lib._SIGNATURES[name]
+        assert (res is ctypes.c_char_p) == (ret == 'const char*'), name
+        params = [] if args.strip() in ('', 'void') else [a for a in args.replace('\n', ' ').split(',')]
+        assert [_c_class(a) for a in params] == [_ctypes_class(t) for t in argtypes], name
+
+
 def test_null_pointers_return_status_and_message():
     lib = _lib.lib()
     rc = lib.fw_add_layernorm(None, None, None, None, None, 1280, 1e-5, None)
