@@ -598,19 +598,23 @@ def bench_ours(args, rank, world, local_rank):
         prompt_ms += ev[2].elapsed_time(ev[3]) / reps
         dec_ms += ev[3].elapsed_time(ev[4]) / reps
     us_per_token = ranks.reduce(dec_ms * 1e3 / dec_steps)
-    # the same steps as one launch of the on-device decode loop (conditional WHILE graph)
-    loop_us = None
-    if model.loop is not None:
+    # the same steps as one launch of the on-device decode loop (conditional WHILE graph): the exact
+    # loop (stop condition after every step) and the chunked one that transcribe(stop_at_eos=True)
+    # uses (after every 8 steps; its last chunk may decode past the limit, counted in the time)
+    loop_us = {}
+    for key, chunked, ok in (('step', False, model.loop is not None), ('chunk', True, model.loop_chunk is not None)):
+        if not ok:
+            continue
         loop_ms = 0.0
         for _ in range(reps):
             model.run_front()
             model.run_prompt()
             ev[3].record(stream)
-            model.run_loop(N_TOKENS, False)
+            model.run_loop(N_TOKENS, False, chunked=chunked)
             ev[4].record(stream)
             torch.cuda.synchronize()
             loop_ms += ev[3].elapsed_time(ev[4]) / reps
-        loop_us = ranks.reduce(loop_ms * 1e3 / dec_steps)
+        loop_us[key] = ranks.reduce(loop_ms * 1e3 / dec_steps)
         assert model.tokens[:N_TOKENS].tolist() == toks, 'decode loop and chunk graphs disagree'
 
     # (3) end to end through the public API: pinned host audio -> host token ids
@@ -661,7 +665,8 @@ def bench_ours(args, rank, world, local_rank):
                 'd2h_bytes_per_step': N_TOKENS * 8},
         'ttft_ms': round(ttft_ms, 4),
         'decode_us_per_token': round(us_per_token, 3),
-        'decode_us_per_token_device_loop': round(loop_us, 3) if loop_us is not None else None,
+        'decode_us_per_token_device_loop': round(loop_us['step'], 3) if 'step' in loop_us else None,
+        'decode_us_per_token_device_loop_chunk8': round(loop_us['chunk'], 3) if 'chunk' in loop_us else None,
         'stages_ms': {'mel': round(mel_ms, 4), 'encoder': round(enc_ms, 4), 'prompt': round(prompt_ms, 4),
                       'decode': round(dec_ms, 4)},
         'throughput_audio_s_per_s': round(world * SECONDS / (step_ms / 1e3), 2),

@@ -2510,12 +2510,19 @@ __global__ void __launch_bounds__(kBfc2Threads, 1) bfc2_residual_kernel(BatchFc2
 // than ctrl[0] tokens were generated, the last generated token is not EOS (when ctrl[2] is set) and
 // the cap is not reached (a guard that makes the loop finite whatever the state holds).
 __global__ void decode_loop_cond_kernel(const int64_t* __restrict__ state, const int64_t* __restrict__ tokens,
-                                        int64_t* __restrict__ ctrl, cudaGraphConditionalHandle handle, int first) {
+                                        int64_t* __restrict__ ctrl, cudaGraphConditionalHandle handle, int first,
+                                        int window) {
   const int64_t it = first ? 0 : ctrl[3] + 1;
   ctrl[3] = it;
   const int64_t n = state[1];
   bool more = n < ctrl[0] && it < ctrl[4];
-  if (more && ctrl[2] != 0 && n > 0 && tokens[n - 1] == ctrl[1]) more = false;
+  // stop at EOS among the tokens the last iteration generated (its `window` steps)
+  if (more && ctrl[2] != 0)
+    for (int64_t i = n > window ? n - window : 0; i < n; ++i)
+      if (tokens[i] == ctrl[1]) {
+        more = false;
+        break;
+      }
   cudaGraphSetConditional(handle, more ? 1u : 0u);
 }
 
@@ -3340,7 +3347,7 @@ int fw_decode_loop_create(const fw_decoder_t* d, int64_t* ctrl, int steps_per_it
   if (e == cudaSuccess) e = cudaStreamBeginCaptureToGraph(s, graph, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed);
   if (e == cudaSuccess) {
     decode_loop_cond_kernel<<<1, 1, 0, s>>>(static_cast<const int64_t*>(d->state), static_cast<const int64_t*>(d->tokens),
-                                           ctrl, handle, 1);
+                                           ctrl, handle, 1, 1);
     e = cudaGetLastError();
     cudaError_t e2 = cudaStreamEndCapture(s, &graph);
     if (e == cudaSuccess) e = e2;
@@ -3364,7 +3371,7 @@ int fw_decode_loop_create(const fw_decoder_t* d, int64_t* ctrl, int steps_per_it
     for (int i = 0; i < steps_per_iter && rc == FW_OK; ++i) rc = decoder_one_step(d, s, nullptr);
     if (rc == FW_OK) {
       decode_loop_cond_kernel<<<1, 1, 0, s>>>(static_cast<const int64_t*>(d->state),
-                                             static_cast<const int64_t*>(d->tokens), ctrl, handle, 0);
+                                             static_cast<const int64_t*>(d->tokens), ctrl, handle, 0, steps_per_iter);
       e = cudaGetLastError();
     }
     cudaError_t e2 = cudaStreamEndCapture(s, &body);

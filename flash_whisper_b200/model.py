@@ -145,7 +145,7 @@ class CustomModel:
         if selftest:
             self.selftest['mel_max_abs_diff'] = self._mel_diff()
         self.graph_mel = self.graph_enc = self.graph_prompt = self.graph_chunk = None
-        self.loop = None
+        self.loop = self.loop_chunk = None
         if capture:
             self._capture()
 
@@ -278,34 +278,43 @@ class CustomModel:
             self.mel.copy_(mel_saved)
         self._make_loop()
 
-    def _make_loop(self, steps_per_iter=1):
-        """The on-device decode loop (fw_decode_loop_*): one graph launch decodes until EOS or the token
-        limit, the stop condition evaluated on the GPU after every step."""
+    def _make_loop(self):
+        """The on-device decode loops (fw_decode_loop_*): one graph launch decodes until EOS or the token
+        limit, the stop condition evaluated on the GPU. `loop` evaluates it after every step (it stops
+        exactly at the limit or the EOS token); `loop_chunk` after every `chunk` steps, like the
+        reference's 8-step graphs (custom/model.py:208-215), which spends a conditional-node iteration
+        per chunk instead of per token and may decode up to chunk - 1 tokens past the stop, which the
+        caller drops. transcribe(stop_at_eos=True) uses `loop_chunk`."""
         self.loop_ctrl = torch.zeros(5, dtype=torch.long, device='cuda')
         self.loop_ctrl_host = torch.zeros(5, dtype=torch.long).pin_memory()
         self._ctrl_copied = None
-        handle = ctypes.c_void_p()
+        self._loop_destroy = _lib.lib().fw_decode_loop_destroy  # held: module globals may be gone at exit
+        self.loop = self.loop_chunk = None
         try:
-            _lib.call('fw_decode_loop_create', ctypes.byref(self.dec_desc), _p(self.loop_ctrl), int(steps_per_iter),
-                      ctypes.byref(handle))
-            self.loop = handle
-            self._loop_destroy = _lib.lib().fw_decode_loop_destroy  # held: module globals may be gone at exit
+            for name, steps in (('loop', 1), ('loop_chunk', self.chunk)):
+                handle = ctypes.c_void_p()
+                _lib.call('fw_decode_loop_create', ctypes.byref(self.dec_desc), _p(self.loop_ctrl), int(steps),
+                          ctypes.byref(handle))
+                setattr(self, name, handle)
             self.selftest['decode_loop'] = True
         except RuntimeError as exc:  # the host loop of chunk graphs is used instead
-            self.loop = None
             self.selftest['decode_loop'] = False
             self.selftest['decode_loop_error'] = str(exc)
 
     def __del__(self):
-        loop, destroy = getattr(self, 'loop', None), getattr(self, '_loop_destroy', None)
-        if loop is not None and destroy is not None:
-            destroy(loop)
-            self.loop = None
+        destroy = getattr(self, '_loop_destroy', None)
+        for name in ('loop', 'loop_chunk'):
+            loop = getattr(self, name, None)
+            if loop is not None and destroy is not None:
+                destroy(loop)
+                setattr(self, name, None)
 
-    def run_loop(self, limit, stop_at_eos, eos=None):
+    def run_loop(self, limit, stop_at_eos, eos=None, chunked=False):
         """Decode steps on the GPU until state[1] (tokens generated) reaches `limit` or, with
         stop_at_eos, the last generated token is `eos` (default: the model's EOS id); one graph
-        launch, no host synchronisation."""
+        launch, no host synchronisation. chunked=True runs `loop_chunk`, which checks the stop only
+        every `chunk` steps (up to chunk - 1 extra tokens, to be dropped by the caller)."""
+        loop = self.loop_chunk if chunked else self.loop
         if self._ctrl_copied is not None:
             self._ctrl_copied.synchronize()
         eos = self.dims.eos_token_id if eos is None else int(eos)
@@ -314,7 +323,7 @@ class CustomModel:
         self.loop_ctrl.copy_(self.loop_ctrl_host, non_blocking=True)
         self._ctrl_copied = torch.cuda.Event()
         self._ctrl_copied.record()
-        _lib.call('fw_decode_loop_launch', self.loop, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        _lib.call('fw_decode_loop_launch', loop, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
     def run_mel(self):
         self.graph_mel.replay() if self.graph_mel else self._mel()
@@ -459,12 +468,13 @@ class CustomModel:
             ttft = time.perf_counter() - start
             stream.synchronize()
             token_ids = self.tokens_host[:limit].tolist()
-        elif self.loop is not None:
+        elif self.loop_chunk is not None:
             # prompt -> first token read back (TTFT) while the on-device loop decodes to EOS / limit
+            # (chunks of `chunk` steps; the tokens past the limit or the first EOS are dropped below)
             self.tokens_host[:1].copy_(self.tokens[:1], non_blocking=True)
             first = torch.cuda.Event()
             first.record(stream)
-            self.run_loop(limit, True)
+            self.run_loop(limit, True, chunked=True)
             self.tokens_host[:limit].copy_(self.tokens[:limit], non_blocking=True)
             state_host = self.state.to('cpu', non_blocking=True)
             first.synchronize()

@@ -234,9 +234,12 @@ typedef struct fw_decode_loop fw_decode_loop_t;
  * launch: ctrl[0] = token limit (stop once state[1] reaches it), ctrl[1] = EOS id, ctrl[2] = 1 to stop
  * after the first EOS token (0 to ignore EOS), ctrl[4] = cap on body iterations (a guard; the loop
  * always ends); ctrl[3] receives the number of body iterations run minus one. Each iteration runs
- * `steps_per_iter` decode steps, then re-evaluates the condition; the condition is also evaluated
- * once before the first iteration. Host-side set-up only: it creates (and destroys) a private
- * stream and the graph, and launches nothing. */
+ * `steps_per_iter` decode steps, then re-evaluates the condition (EOS is looked for among the
+ * tokens of the whole iteration); the condition is also evaluated once before the first iteration.
+ * With steps_per_iter > 1 the last iteration may generate up to steps_per_iter - 1 tokens past the
+ * limit or the EOS token, as the reference's 8-step chunks do (custom/model.py:208-215): the caller
+ * keeps the first min(state[1], limit) tokens up to the first EOS. Host-side set-up only: it
+ * creates (and destroys) a private stream and the graph, and launches nothing. */
 int fw_decode_loop_create(const fw_decoder_t* d, int64_t* ctrl, int steps_per_iter, fw_decode_loop_t** out);
 /* Launches the loop on `stream` (asynchronous; one graph launch). */
 int fw_decode_loop_launch(fw_decode_loop_t* loop, fw_stream_t stream);
