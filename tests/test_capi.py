@@ -144,3 +144,18 @@ def test_model_requires_cuda_without_fallback():
     from flash_whisper_b200.model import CustomModel
     with pytest.raises(RuntimeError, match='requires a CUDA device'):
         CustomModel()
+
+
+def test_audio_checks_match_the_reference():
+    """transcribe's input checks (custom/model.py:175-178), which run before anything touches the GPU:
+    a 1-D float32 array of 1..480000 finite samples, ValueError otherwise."""
+    import numpy as np
+    from flash_whisper_b200.model import CustomModel
+    check = CustomModel._check_audio
+    check(np.zeros(1, np.float32))
+    check(np.zeros(480000, np.float32))
+    bad = [np.zeros(16000, np.float64), np.zeros((2, 8000), np.float32), [0.0] * 16000, np.zeros(0, np.float32),
+           np.zeros(480001, np.float32), np.array([0.0, np.nan], np.float32), np.array([np.inf], np.float32)]
+    for audio in bad:
+        with pytest.raises(ValueError):
+            check(audio)
